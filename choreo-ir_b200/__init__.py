@@ -1,0 +1,270 @@
+"""ctypes binding of libchoreo_b200.so (the C ABI in include/choreo_b200.h).
+
+This module is how Python code (tests, bench.py, __graft_entry__) reaches the
+CUDA kernels. It calls the C ABI with raw device pointers; torch tensors are
+accepted as a convenience for owning device memory and streams, nothing more.
+Every non-zero status raises RuntimeError with the library's message, the way
+the reference's C++ API throws std::runtime_error.
+
+The library must have been built (choreo-ir_b200/build.py); importing this
+module without it raises immediately: there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libchoreo_b200.so"
+
+F16, F32, BF16 = 8, 9, 11
+OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_WORKSPACE = 0, -1, -2, -3, -4, -5
+
+
+class GemmDesc(C.Structure):
+    _fields_ = [
+        ("m", C.c_int64), ("n", C.c_int64), ("k", C.c_int64),
+        ("dtype_ab", C.c_int32), ("dtype_c", C.c_int32),
+        ("a", C.c_void_p), ("lda", C.c_int64), ("trans_a", C.c_int32),
+        ("b", C.c_void_p), ("ldb", C.c_int64), ("trans_b", C.c_int32),
+        ("c", C.c_void_p), ("ldc", C.c_int64),
+        ("alpha", C.c_float), ("beta", C.c_float),
+        ("bias", C.c_void_p), ("dtype_bias", C.c_int32),
+        ("relu", C.c_int32),
+        ("batch", C.c_int64), ("stride_a", C.c_int64), ("stride_b", C.c_int64), ("stride_c", C.c_int64),
+    ]
+
+
+class LaunchConfig(C.Structure):
+    _fields_ = [
+        ("kernel", C.c_int32), ("tile_m", C.c_int32), ("tile_n", C.c_int32), ("tile_k", C.c_int32),
+        ("stages", C.c_int32), ("cluster_m", C.c_int32),
+        ("grid_x", C.c_int32), ("grid_y", C.c_int32), ("grid_z", C.c_int32),
+        ("block_x", C.c_int32), ("smem_bytes", C.c_int32), ("tmem_cols", C.c_int32),
+        ("tiles", C.c_int64), ("workspace_bytes", C.c_int64),
+    ]
+
+
+class ConvDesc(C.Structure):
+    _fields_ = [
+        ("n", C.c_int64), ("h", C.c_int64), ("w", C.c_int64), ("c", C.c_int64),
+        ("k", C.c_int64), ("r", C.c_int64), ("s", C.c_int64),
+        ("stride_h", C.c_int32), ("stride_w", C.c_int32),
+        ("pad_h", C.c_int32), ("pad_w", C.c_int32),
+        ("dil_h", C.c_int32), ("dil_w", C.c_int32),
+        ("dtype", C.c_int32), ("dtype_out", C.c_int32),
+        ("input", C.c_void_p), ("weight", C.c_void_p), ("output", C.c_void_p),
+        ("bias", C.c_void_p), ("dtype_bias", C.c_int32), ("relu", C.c_int32),
+        ("alpha", C.c_float),
+    ]
+
+
+class DeviceProps(C.Structure):
+    _fields_ = [
+        ("device", C.c_int32), ("cc_major", C.c_int32), ("cc_minor", C.c_int32),
+        ("sm_count", C.c_int32), ("max_smem_optin", C.c_int32), ("cluster_launch", C.c_int32),
+        ("total_mem", C.c_int64), ("name", C.c_char * 256),
+    ]
+
+
+# Every symbol include/choreo_b200.h declares, with its ctypes signature.
+_SIGNATURES = {
+    "choreo_version": (C.c_int, []),
+    "choreo_last_error": (C.c_char_p, []),
+    "choreo_device_props_get": (C.c_int, [C.c_int, C.POINTER(DeviceProps)]),
+    "choreo_sync_status": (C.c_int, [C.c_void_p]),
+    "choreo_gemm_query": (C.c_int, [C.POINTER(GemmDesc), C.POINTER(LaunchConfig)]),
+    "choreo_gemm": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "choreo_gemm_rowsharded": (C.c_int, [C.POINTER(GemmDesc), C.c_int, C.POINTER(C.c_int),
+                                         C.POINTER(C.c_void_p), C.POINTER(C.c_float)]),
+    "choreo_shard_rows": (C.c_int, [C.c_int64, C.c_int, C.c_int, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
+    "choreo_conv2d_query": (C.c_int, [C.POINTER(ConvDesc), C.POINTER(LaunchConfig)]),
+    "choreo_conv2d": (C.c_int, [C.POINTER(ConvDesc), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "choreo_relu": (C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
+    "choreo_add": (C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
+    "choreo_fill": (C.c_int, [C.c_int32, C.c_void_p, C.c_double, C.c_int64, C.c_void_p]),
+    "choreo_convert": (C.c_int, [C.c_int32, C.c_void_p, C.c_int32, C.c_void_p, C.c_int64, C.c_void_p]),
+}
+
+
+def _load() -> C.CDLL:
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `python choreo-ir_b200/build.py`")
+    lib = C.CDLL(str(LIB_PATH))
+    for name, (res, args) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+class ChoreoError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+def check(rc: int) -> None:
+    if rc != 0:
+        raise ChoreoError(rc, lib.choreo_last_error().decode())
+
+
+def _ptr(x) -> int | None:
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    return x.data_ptr()
+
+
+_TORCH_DT = {}
+
+
+def dtype_code(t) -> int:
+    """Library dtype code of a torch tensor."""
+    import torch
+    if not _TORCH_DT:
+        _TORCH_DT.update({torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32})
+    return _TORCH_DT[t.dtype]
+
+
+def _stream_ptr(stream) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def make_gemm_desc(a, b, c, *, m, n, k, trans_a=False, trans_b=False, lda=None, ldb=None, ldc=None,
+                   alpha=1.0, beta=0.0, bias=None, relu=False, batch=1,
+                   stride_a=0, stride_b=0, stride_c=0, dtype_ab=None, dtype_c=None, dtype_bias=None) -> GemmDesc:
+    d = GemmDesc()
+    d.m, d.n, d.k = m, n, k
+    d.dtype_ab = dtype_ab if dtype_ab is not None else dtype_code(a)
+    d.dtype_c = dtype_c if dtype_c is not None else dtype_code(c)
+    d.a, d.b, d.c = _ptr(a), _ptr(b), _ptr(c)
+    d.trans_a, d.trans_b = int(trans_a), int(trans_b)
+    d.lda = lda if lda is not None else (m if trans_a else k)
+    d.ldb = ldb if ldb is not None else (k if trans_b else n)
+    d.ldc = ldc if ldc is not None else n
+    d.alpha, d.beta = alpha, beta
+    d.bias = _ptr(bias)
+    d.dtype_bias = dtype_bias if dtype_bias is not None else (dtype_code(bias) if bias is not None and not isinstance(bias, int) else F32)
+    d.relu = int(relu)
+    d.batch, d.stride_a, d.stride_b, d.stride_c = batch, stride_a, stride_b, stride_c
+    return d
+
+
+def gemm_query(d: GemmDesc) -> LaunchConfig:
+    out = LaunchConfig()
+    check(lib.choreo_gemm_query(C.byref(d), C.byref(out)))
+    return out
+
+
+def gemm_desc(d: GemmDesc, workspace=None, workspace_bytes=0, stream=None) -> None:
+    check(lib.choreo_gemm(C.byref(d), _ptr(workspace), workspace_bytes, _stream_ptr(stream)))
+
+
+def gemm(a, b, c, *, trans_a=False, trans_b=False, alpha=1.0, beta=0.0, bias=None, relu=False,
+         workspace=None, stream=None) -> None:
+    """C = act(alpha * op(A) op(B) + beta * C + bias) on 2-D (or 3-D batched) torch tensors.
+
+    a is M x K (K x M if trans_a), b is K x N (N x K if trans_b); rows may be
+    padded (the row stride is taken as the leading dimension)."""
+    batched = a.dim() == 3
+    if batched:
+        batch = a.shape[0]
+        sa, sb, sc = a.stride(0), b.stride(0) if b.dim() == 3 else 0, c.stride(0)
+        a2, b2, c2 = a[0], (b[0] if b.dim() == 3 else b), c[0]
+    else:
+        batch, sa, sb, sc = 1, 0, 0, 0
+        a2, b2, c2 = a, b, c
+    m = a2.shape[1] if trans_a else a2.shape[0]
+    k = a2.shape[0] if trans_a else a2.shape[1]
+    n = b2.shape[0] if trans_b else b2.shape[1]
+    for t in (a2, b2, c2):
+        if t.stride(-1) != 1:
+            raise ValueError("innermost dimension must be contiguous")
+    d = make_gemm_desc(a, b, c, m=m, n=n, k=k, trans_a=trans_a, trans_b=trans_b,
+                       lda=a2.stride(0), ldb=b2.stride(0), ldc=c2.stride(0), alpha=alpha, beta=beta,
+                       bias=bias, relu=relu, batch=batch, stride_a=sa, stride_b=sb, stride_c=sc)
+    ws_bytes = 0
+    if workspace is None:
+        need = gemm_query(d).workspace_bytes
+        if need:
+            import torch
+            workspace = torch.empty(need, dtype=torch.uint8, device=c.device)
+    if workspace is not None:
+        ws_bytes = workspace.numel() * workspace.element_size()
+    gemm_desc(d, workspace, ws_bytes, stream)
+
+
+def conv_desc(x, w, out, *, stride=1, padding=1, dilation=1, bias=None, relu=False, alpha=1.0) -> ConvDesc:
+    """x: NHWC, w: KRSC, out: NHWC (torch tensors, contiguous)."""
+    d = ConvDesc()
+    d.n, d.h, d.w, d.c = x.shape
+    d.k, d.r, d.s = w.shape[0], w.shape[1], w.shape[2]
+    d.stride_h = d.stride_w = stride
+    d.pad_h = d.pad_w = padding
+    d.dil_h = d.dil_w = dilation
+    d.dtype, d.dtype_out = dtype_code(x), dtype_code(out)
+    d.input, d.weight, d.output = x.data_ptr(), w.data_ptr(), out.data_ptr()
+    d.bias = _ptr(bias)
+    d.dtype_bias = dtype_code(bias) if bias is not None else F32
+    d.relu = int(relu)
+    d.alpha = alpha
+    return d
+
+
+def conv2d_query(d: ConvDesc) -> LaunchConfig:
+    out = LaunchConfig()
+    check(lib.choreo_conv2d_query(C.byref(d), C.byref(out)))
+    return out
+
+
+def conv2d(x, w, out, *, stride=1, padding=1, dilation=1, bias=None, relu=False, alpha=1.0, stream=None) -> None:
+    d = conv_desc(x, w, out, stride=stride, padding=padding, dilation=dilation, bias=bias, relu=relu, alpha=alpha)
+    check(lib.choreo_conv2d(C.byref(d), None, 0, _stream_ptr(stream)))
+
+
+def relu(x, out, stream=None) -> None:
+    check(lib.choreo_relu(dtype_code(x), x.data_ptr(), out.data_ptr(), x.numel(), _stream_ptr(stream)))
+
+
+def add(a, b, out, stream=None) -> None:
+    check(lib.choreo_add(dtype_code(a), a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(), _stream_ptr(stream)))
+
+
+def fill(x, value: float, stream=None) -> None:
+    check(lib.choreo_fill(dtype_code(x), x.data_ptr(), float(value), x.numel(), _stream_ptr(stream)))
+
+
+def convert(src, dst, stream=None) -> None:
+    check(lib.choreo_convert(dtype_code(src), src.data_ptr(), dtype_code(dst), dst.data_ptr(), src.numel(),
+                             _stream_ptr(stream)))
+
+
+def sync_status(stream=None) -> None:
+    check(lib.choreo_sync_status(_stream_ptr(stream)))
+
+
+def shard_rows(m: int, nshards: int, rank: int) -> tuple[int, int]:
+    r0, rows = C.c_int64(), C.c_int64()
+    check(lib.choreo_shard_rows(m, nshards, rank, C.byref(r0), C.byref(rows)))
+    return r0.value, rows.value
+
+
+def device_props(device: int = 0) -> DeviceProps:
+    p = DeviceProps()
+    check(lib.choreo_device_props_get(device, C.byref(p)))
+    return p
+
+
+def version() -> int:
+    return lib.choreo_version()

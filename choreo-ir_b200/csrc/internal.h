@@ -1,0 +1,86 @@
+// internal.h — declarations shared by the translation units of libchoreo_b200.so.
+// Not installed; the public surface is include/choreo_b200.h.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstddef>
+
+#include "../../include/choreo_b200.h"
+
+namespace choreo_impl {
+
+// Records `msg` as this host thread's last error and returns `code`.
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+// Clears the last error and returns CHOREO_OK.
+int ok();
+// Converts a CUDA runtime error into CHOREO_ERR_CUDA with context.
+int cuda_fail(cudaError_t e, const char* what);
+
+// Device status word of the current device (kernel-side failure record).
+uint32_t* status_word();
+// Per-wait time limit handed to kernels, in nanoseconds.
+uint64_t wait_timeout_ns();
+// SM count and opt-in shared memory of the current device (cached).
+int current_sm_count();
+int current_smem_optin();
+
+// 16-bit element tensor-map encoding (TMA, SWIZZLE_128B, zero OOB fill).
+// dims/strides follow cuTensorMapEncodeTiled: dims[0] innermost; strides in
+// bytes for dims[1..rank-1].
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+                const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                CUtensorMapSwizzle swizzle);
+
+// ---------------------------------------------------------------- GEMM
+// Tile configurations of the tcgen05 GEMM (BM = 128, BK = 64).
+struct TcConfig {
+  int bn;       // 64, 128 or 256
+  int stages;   // shared-memory pipeline depth
+  int smem;     // dynamic shared memory bytes
+  int group_m;  // rasterisation group (M tiles walked together for L2 reuse)
+};
+TcConfig select_tc_config(int64_t m, int64_t n, int64_t k, int64_t batch, int sm_count);
+
+// A GEMM with every operand already TMA-legal (16-byte aligned base, ld and
+// batch stride), in the orientation it is stored.
+struct TcProblem {
+  int64_t m, n, k, batch;
+  bool bf16;                 // A/B are bf16 (else f16)
+  const void* a; int64_t lda; int64_t stride_a; bool a_mn;   // a_mn: A stored K x M
+  const void* b; int64_t ldb; int64_t stride_b; bool b_mn;   // b_mn: B stored K x N
+  void* c; int64_t ldc; int64_t stride_c; int dtype_c;
+  float alpha, beta;
+  const void* bias; int dtype_bias;
+  int relu;
+};
+int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream);
+
+// CUDA-core f32 GEMM (A/B/C f32), any strides.
+int launch_gemm_f32(const choreo_gemm_desc& d, cudaStream_t stream);
+
+// Strided copy of a batch of rows x cols 16-bit matrices (used to repack an
+// operand whose leading dimension or base is not 16-byte aligned).
+int launch_repack16(const void* src, int64_t ld_src, int64_t stride_src, void* dst,
+                    int64_t ld_dst, int64_t stride_dst, int64_t rows, int64_t cols,
+                    int64_t batch, cudaStream_t stream);
+
+// ---------------------------------------------------------------- conv
+int conv_query(const choreo_conv_desc& d, choreo_launch_config* out);
+int launch_conv_tc(const choreo_conv_desc& d, cudaStream_t stream);
+
+// ---------------------------------------------------------------- elementwise
+int launch_relu(int dtype, const void* in, void* out, int64_t n, cudaStream_t s);
+int launch_add(int dtype, const void* a, const void* b, void* out, int64_t n, cudaStream_t s);
+int launch_fill(int dtype, void* dst, double v, int64_t n, cudaStream_t s);
+int launch_convert(int dsrc, const void* src, int ddst, void* dst, int64_t n, cudaStream_t s);
+
+inline int dtype_bytes(int dt) {
+  switch (dt) {
+    case CHOREO_DTYPE_F16: case CHOREO_DTYPE_BF16: return 2;
+    case CHOREO_DTYPE_F32: return 4;
+    default: return 0;
+  }
+}
+
+}  // namespace choreo_impl

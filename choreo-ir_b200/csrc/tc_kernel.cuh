@@ -1,0 +1,350 @@
+// tc_kernel.cuh — the persistent, warp-specialised tcgen05 mainloop shared by
+// the GEMM and the implicit-GEMM convolution.
+//
+// CTA = 6 warps (192 threads), one CTA per SM, grid = min(tiles, SMs):
+//   warp 0       TMA producer: fills a STAGES-deep ring of shared-memory
+//                stages (A tile 128 x 64, B tile BN x 64, 128-byte swizzle).
+//   warp 1       allocates 2*BN TMEM columns (two fp32 accumulators), and one
+//                elected lane issues tcgen05.mma (128 x BN x 16 per
+//                instruction, 4 per stage), releasing each stage with
+//                tcgen05.commit and signalling a finished accumulator.
+//   warps 2..5   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
+//                32*(w%4)..+31 = tile rows), apply alpha/beta/bias/ReLU, cast
+//                and store with 16-byte vector stores. Accumulators are double
+//                buffered so the epilogue of tile i overlaps the MMAs of i+1.
+// Tiles are walked in groups of `group_m` M-tiles so concurrently running
+// CTAs share A and B panels in L2.
+//
+// Every mbarrier wait is bounded (see sm100.cuh): a stuck pipeline records an
+// error in the device status word and the kernel returns.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "sm100.cuh"
+
+namespace choreo_sm100 {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;
+
+// Everything the kernel needs besides the two tensor maps.
+struct TcParams {
+  int32_t m, n;            // output rows / columns (per batch item)
+  int32_t num_k_blocks;    // K / 64 rounded up (conv: R*S*ceil(C/64))
+  int32_t num_m_blocks, num_n_blocks;
+  int32_t batch;
+  int64_t num_tiles;
+  int32_t group_m;
+  int32_t ab_bf16;
+  // epilogue
+  void* c;
+  int64_t ldc, stride_c;   // elements
+  int32_t c_vec_ok;        // 16-byte vector stores are legal for C
+  float alpha, beta;
+  const void* bias;
+  int32_t dtype_bias;      // 8 f16, 9 f32, 11 bf16
+  int32_t relu;
+  // convolution geometry (loader-specific)
+  int32_t conv_c_blocks;   // ceil(C / 64)
+  int32_t conv_s;          // filter width
+  int32_t conv_q, conv_p;  // output width / height
+  int32_t conv_pad_w, conv_pad_h;
+  int32_t conv_stride_w, conv_stride_h;
+  int32_t conv_dil_w, conv_dil_h;
+  // failure reporting
+  uint32_t* status;
+  uint64_t timeout_ns;
+};
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float load_bias(const void* bias, int dt, int idx) {
+  if (dt == 9) return __ldg(static_cast<const float*>(bias) + idx);
+  if (dt == 11) return __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[idx]);
+  return __half2float(static_cast<const __half*>(bias)[idx]);
+}
+
+// Maps a linear tile index to (batch item, M tile, N tile) with grouped
+// rasterisation.
+__device__ __forceinline__ void tile_coords(int64_t t, const TcParams& p, int& b, int& mb, int& nb) {
+  const int64_t per_batch = static_cast<int64_t>(p.num_m_blocks) * p.num_n_blocks;
+  b = static_cast<int>(t / per_batch);
+  const int r = static_cast<int>(t - static_cast<int64_t>(b) * per_batch);
+  const int tiles_per_group = p.group_m * p.num_n_blocks;
+  const int g = r / tiles_per_group;
+  const int first_m = g * p.group_m;
+  const int gm = min(p.num_m_blocks - first_m, p.group_m);
+  const int in = r - g * tiles_per_group;
+  mb = first_m + in % gm;
+  nb = in / gm;
+}
+
+// Epilogue for one 32-column chunk of one row held by this thread.
+template <typename OutT>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], OutT* crow, int n_base,
+                                               const TcParams& p, bool row_ok) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+  const bool full = (n_base + 32 <= p.n);
+  if (p.beta != 0.f && row_ok) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (full || n_base + i < p.n) v[i] += p.beta * to_f32<OutT>(crow[n_base + i]);
+  }
+  if (p.bias != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (full || n_base + i < p.n) v[i] += load_bias(p.bias, p.dtype_bias, n_base + i);
+  }
+  if (p.relu) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = (v[i] < 0.f) ? 0.f : v[i];  // NaN passes, like std::max(x, 0)
+  }
+  if (!row_ok) return;
+  if constexpr (sizeof(OutT) == 2) {
+    if (full && p.c_vec_ok) {
+      uint4* dst = reinterpret_cast<uint4*>(crow + n_base);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 q;
+        q.x = pack2(v[8 * j + 0], v[8 * j + 1], static_cast<OutT*>(nullptr));
+        q.y = pack2(v[8 * j + 2], v[8 * j + 3], static_cast<OutT*>(nullptr));
+        q.z = pack2(v[8 * j + 4], v[8 * j + 5], static_cast<OutT*>(nullptr));
+        q.w = pack2(v[8 * j + 6], v[8 * j + 7], static_cast<OutT*>(nullptr));
+        dst[j] = q;
+      }
+      return;
+    }
+  } else {
+    if (full && p.c_vec_ok) {
+      float4* dst = reinterpret_cast<float4*>(crow + n_base);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        dst[j] = make_float4(v[4 * j + 0], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      return;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    if (n_base + i < p.n) crow[n_base + i] = from_f32<OutT>(v[i]);
+}
+
+// Shared-memory bookkeeping beyond the stage ring.
+template <int STAGES>
+struct alignas(8) TcBarriers {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int32_t abort;
+};
+
+template <int BN, int STAGES>
+constexpr int tc_smem_bytes() {
+  return STAGES * (kBM * kBK * 2 + BN * kBK * 2) + 1024 /*alignment slack*/ +
+         static_cast<int>(sizeof(TcBarriers<STAGES>));
+}
+
+// Loader contract:
+//   static constexpr bool kAMn, kBMn;          operand majorness in shared memory
+//   __device__ static void issue(const CUtensorMap* ta, const CUtensorMap* tb, const TcParams&,
+//                                int b, int mb, int nb, int kb, uint32_t dst_a, uint32_t dst_b,
+//                                uint32_t bar, uint64_t pol_a, uint64_t pol_b);
+template <int BN, int STAGES, class Loader, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
+                   const __grid_constant__ CUtensorMap tma_b, const TcParams p) {
+  constexpr uint32_t kAStage = kBM * kBK * 2;
+  constexpr uint32_t kBStage = BN * kBK * 2;
+  constexpr uint32_t kStageBytes = kAStage + kBStage;
+  constexpr uint32_t kTmemCols = 2 * BN;
+  static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* s_a = smem;
+  uint8_t* s_b = smem + STAGES * kAStage;
+  auto* bars = reinterpret_cast<TcBarriers<STAGES>*>(s_b + STAGES * kBStage);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&bars->full[s]), 1);
+      mbar_init(smem_u32(&bars->empty[s]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&bars->tmem_full[i]), 1);
+      mbar_init(smem_u32(&bars->tmem_empty[i]), 4);
+    }
+    mbar_init(smem_u32(&bars->drain), 1);
+    bars->abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&bars->tmem_base), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+  const WaitCtx wctx{p.status, p.timeout_ns, &bars->abort};
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_a = l2_policy_evict_normal();
+      const uint64_t pol_b = l2_policy_evict_last();
+      uint32_t stage = 0, phase = 0, issued = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int b, mb, nb;
+        tile_coords(t, p, b, mb, nb);
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(&bars->empty[stage]), phase ^ 1, wctx, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&bars->full[stage]);
+          mbar_arrive_expect_tx(fb, kStageBytes);
+          Loader::issue(&tma_a, &tma_b, p, b, mb, nb, kb, smem_u32(s_a + stage * kAStage),
+                        smem_u32(s_b + stage * kBStage), fb, pol_a, pol_b);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        // Let the loads already in flight land before the CTA exits.
+        const uint32_t inflight = issued < STAGES ? issued : STAGES;
+        uint32_t s = stage, ph = phase;
+        for (uint32_t i = 0; i < inflight; ++i) {
+          if (s == 0) { s = STAGES - 1; ph ^= 1; } else { --s; }
+          mbar_wait(smem_u32(&bars->full[s]), ph, wctx, kStatusTimeoutDrain, false);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(kBM, BN, p.ab_bf16 != 0, Loader::kAMn, Loader::kBMn);
+      uint32_t stage = 0, phase = 0, local = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
+        const uint32_t buf = local & 1;
+        const uint32_t tph = (local >> 1) & 1;
+        if (!mbar_wait(smem_u32(&bars->tmem_empty[buf]), tph ^ 1, wctx, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(&bars->full[stage]), phase, wctx, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(s_a + stage * kAStage);
+          const uint32_t b0 = smem_u32(s_b + stage * kBStage);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = Loader::kAMn ? smem_desc_sw128(a0 + k * 2048, 8192, 1024)
+                                             : smem_desc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bd = Loader::kBMn ? smem_desc_sw128(b0 + k * 2048, 8192, 1024)
+                                             : smem_desc_sw128(b0 + k * 32, 16, 1024);
+            umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(smem_u32(&bars->empty[stage]));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&bars->tmem_full[buf]));
+      }
+      // All MMAs must have finished before TMEM is released.
+      umma_commit(smem_u32(&bars->drain));
+      mbar_wait(smem_u32(&bars->drain), 0, wctx, kStatusTimeoutDrain, false);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes this warp may read
+    uint32_t local = 0;
+    for (int64_t t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+      const uint32_t buf = local & 1;
+      const uint32_t tph = (local >> 1) & 1;
+      int ready = 0;
+      if (lane == 0)
+        ready = mbar_wait(smem_u32(&bars->tmem_full[buf]), tph, wctx, kStatusTimeoutEpilogue) ? 1 : 0;
+      ready = __shfl_sync(0xffffffffu, ready, 0);
+      if (!ready) break;
+      tc_fence_after();
+      int b, mb, nb;
+      tile_coords(t, p, b, mb, nb);
+      const int row = mb * kBM + quarter * 32 + lane;
+      const bool row_ok = row < p.m;
+      OutT* crow = static_cast<OutT*>(p.c) + static_cast<int64_t>(b) * p.stride_c +
+                   static_cast<int64_t>(row_ok ? row : 0) * p.ldc;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int n_base = nb * BN + c * 32;
+        if (n_base >= p.n) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        tmem_wait_ld();
+        epilogue_chunk<OutT>(r, crow, n_base, p, row_ok);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars->tmem_empty[buf]));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace choreo_sm100

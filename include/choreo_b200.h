@@ -1,0 +1,213 @@
+/*
+ * choreo_b200.h — C ABI of the B200 (sm_100a) dense-contraction library.
+ *
+ * Plain pointers, sizes and status codes only: no CUDA, C++ or Python types
+ * appear in the signatures (streams are passed as `void*`, i.e. a
+ * cudaStream_t or NULL for the legacy default stream). The library never owns
+ * caller memory: every device pointer below is allocated and freed by the
+ * caller, who keeps ownership.
+ *
+ * The reference (codes1gn/choreo-ir) is a header-only C++ library with no C
+ * ABI; each entry point names the reference interface it stands behind. The
+ * C++ front end in include/choreo-ir/ calls these functions and rethrows
+ * non-zero status codes as std::runtime_error with the message from
+ * choreo_last_error(), which is what the reference's callers expect.
+ *
+ * Error convention: 0 = success, negative = failure (see choreo_status).
+ * Launch-time checks are synchronous; failures inside a kernel (a pipeline
+ * wait that ran out of time) are recorded in a per-device status word and
+ * reported by choreo_sync_status().
+ */
+#ifndef CHOREO_B200_H
+#define CHOREO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+typedef enum choreo_status {
+  CHOREO_OK = 0,
+  CHOREO_ERR_INVALID_ARG = -1,  /* shape/dtype/pointer contract violated */
+  CHOREO_ERR_UNSUPPORTED = -2,  /* valid request this build does not implement */
+  CHOREO_ERR_CUDA = -3,         /* a CUDA runtime/driver call failed */
+  CHOREO_ERR_TIMEOUT = -4,      /* a kernel pipeline wait expired (see choreo_sync_status) */
+  CHOREO_ERR_WORKSPACE = -5     /* workspace missing or smaller than the queried size */
+} choreo_status;
+
+/* Element types. Values equal the reference's DataType enum
+ * (include/choreo-ir/core/types.hpp:58-71) so the C++ front end can pass
+ * Tensor<T>::dtype() straight through. */
+typedef enum choreo_dtype {
+  CHOREO_DTYPE_F16 = 8,
+  CHOREO_DTYPE_F32 = 9,
+  CHOREO_DTYPE_BF16 = 11
+} choreo_dtype;
+
+/* One (optionally batched) GEMM:
+ *   C[b] = act(alpha * op(A[b]) * op(B[b]) + beta * C[b] + bias)
+ * op(A) is M x K: trans_a == 0 -> A stored M x K row-major with leading
+ * dimension lda (>= K); trans_a == 1 -> A stored K x M row-major (lda >= M).
+ * op(B) is K x N: trans_b == 0 -> B stored K x N row-major (ldb >= N);
+ * trans_b == 1 -> B stored N x K row-major (ldb >= K).
+ * C is M x N row-major with leading dimension ldc (>= N).
+ * bias (optional, may be NULL) is an N-vector broadcast over rows.
+ * act is ReLU when relu != 0, identity otherwise.
+ * batch >= 1; stride_* are element strides between consecutive batch items
+ * (ignored when batch == 1).
+ * Supported types: A/B f16 or bf16 (tensor cores, fp32 accumulation) with C
+ * f16, bf16 or f32; or A/B/C all f32 (CUDA cores, fp32 accumulation). */
+typedef struct choreo_gemm_desc {
+  int64_t m, n, k;
+  int32_t dtype_ab;
+  int32_t dtype_c;
+  const void* a;
+  int64_t lda;
+  int32_t trans_a;
+  const void* b;
+  int64_t ldb;
+  int32_t trans_b;
+  void* c;
+  int64_t ldc;
+  float alpha;
+  float beta;
+  const void* bias;
+  int32_t dtype_bias;
+  int32_t relu;
+  int64_t batch;
+  int64_t stride_a, stride_b, stride_c;
+} choreo_gemm_desc;
+
+/* The kernel configuration the dispatcher picks for a request (backs the
+ * reference's get_optimal_gemm_config, compute/compute_impl.hpp:74-91, and the
+ * auto_analyze() of examples/ideal_matmul_example.cu:244-290). */
+typedef struct choreo_launch_config {
+  int32_t kernel;          /* 1 = tcgen05 tile GEMM, 2 = CUDA-core f32 GEMM, 3 = tcgen05 conv */
+  int32_t tile_m, tile_n, tile_k;
+  int32_t stages;          /* shared-memory pipeline depth */
+  int32_t cluster_m;       /* CTAs per cluster along M (1 = no cluster) */
+  int32_t grid_x, grid_y, grid_z;
+  int32_t block_x;         /* threads per CTA */
+  int32_t smem_bytes;      /* dynamic shared memory per CTA */
+  int32_t tmem_cols;       /* tensor-memory columns per CTA */
+  int64_t tiles;           /* output tiles (all batch items) */
+  int64_t workspace_bytes; /* device scratch the call needs (0 = none) */
+} choreo_launch_config;
+
+/* Implicit-GEMM 2-D convolution, NHWC activations, KRSC weights:
+ *   out[n,p,q,k] = act(alpha * sum_{r,s,c} in[n, p*stride_h - pad_h + r*dil_h,
+ *                                              q*stride_w - pad_w + s*dil_w, c]
+ *                                         * w[k,r,s,c] + bias[k])
+ * with zero padding. out is NHWC [n, P, Q, k_out]. */
+typedef struct choreo_conv_desc {
+  int64_t n, h, w, c;          /* input NHWC */
+  int64_t k, r, s;             /* output channels, filter height, width */
+  int32_t stride_h, stride_w;
+  int32_t pad_h, pad_w;
+  int32_t dil_h, dil_w;
+  int32_t dtype;               /* input/weight type: f16 or bf16 */
+  int32_t dtype_out;           /* f16, bf16 or f32 */
+  const void* input;
+  const void* weight;
+  void* output;
+  const void* bias;            /* optional K-vector */
+  int32_t dtype_bias;
+  int32_t relu;
+  float alpha;
+} choreo_conv_desc;
+
+/* Device properties the dispatcher uses (backs core/device.hpp:233-269). */
+typedef struct choreo_device_props {
+  int32_t device;
+  int32_t cc_major, cc_minor;
+  int32_t sm_count;
+  int32_t max_smem_optin;      /* bytes of shared memory a CTA may opt into */
+  int32_t cluster_launch;      /* 1 if thread-block clusters are supported */
+  int64_t total_mem;
+  char name[256];
+} choreo_device_props;
+
+/* ---- library / device ------------------------------------------------- */
+
+/* Library version as major*10000 + minor*100 + patch. */
+int choreo_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* choreo_last_error(void);
+
+/* Fills *out for `device`. Replaces DeviceManager::query_device_info
+ * (core/device.hpp:233-269), which maps sm_100 to SM_70. */
+int choreo_device_props_get(int device, choreo_device_props* out);
+
+/* Synchronizes `stream` and reports kernel-side failures recorded since the
+ * last call (CHOREO_ERR_TIMEOUT), clearing the record; CHOREO_ERR_CUDA if the
+ * stream itself reports an error. */
+int choreo_sync_status(void* stream);
+
+/* ---- GEMM ------------------------------------------------------------- */
+
+/* Validates `d` and reports the kernel configuration and workspace size.
+ * Replaces compute::get_optimal_gemm_config (compute/compute_impl.hpp:74-91). */
+int choreo_gemm_query(const choreo_gemm_desc* d, choreo_launch_config* out);
+
+/* Enqueues the GEMM on `stream`. Replaces compute::gemm
+ * (compute/compute_impl.hpp:19-38, declared compute/compute.hpp:55-58) and,
+ * with alpha=1, beta=0, compute::matmul (compute_impl.hpp:52-72) and the
+ * device branch of operator* (choreo-ir.hpp:53-71).
+ * `workspace` must hold choreo_gemm_query(...).workspace_bytes bytes of device
+ * memory (it is used when a stride or base address is not 16-byte aligned, so
+ * the operand is first repacked). */
+int choreo_gemm(const choreo_gemm_desc* d, void* workspace, size_t workspace_bytes,
+                void* stream);
+
+/* Row-sharded GEMM over several GPUs of one process: descs[i] describes
+ * device devices[i]'s slab (its own A rows, its replica of B and bias, its C
+ * rows). One host thread per device launches on streams[i] (NULL = default
+ * stream) and, if ms_out != NULL, synchronizes and stores that device's
+ * kernel time in ms_out[i]. No data crosses between devices. Stands behind
+ * the multi-GPU split of north-star item (5); the reference has no
+ * multi-GPU code (core/device.hpp:136-156 only switches devices). */
+int choreo_gemm_rowsharded(const choreo_gemm_desc* descs, int ngpu, const int* devices,
+                           void* const* streams, float* ms_out);
+
+/* Rows [*row0, *row0 + *rows) of an M-row problem that shard `rank` of
+ * `nshards` owns: contiguous slabs, sizes differing by at most one tile of
+ * 128 rows, earlier shards taking the larger slabs. */
+int choreo_shard_rows(int64_t m, int nshards, int rank, int64_t* row0, int64_t* rows);
+
+/* ---- convolution ------------------------------------------------------- */
+
+int choreo_conv2d_query(const choreo_conv_desc* d, choreo_launch_config* out);
+
+/* Enqueues the implicit-GEMM convolution. Stands behind the conv2d() the
+ * reference's benchmarks call (benchmark/performance/benchmark_suite.cpp:379)
+ * with the semantics of benchmark/kernels/gemm_example.cu:208-253, in NHWC. */
+int choreo_conv2d(const choreo_conv_desc* d, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+/* ---- elementwise (device kernels replacing host round trips) ---------- */
+
+/* out[i] = max(in[i], 0). Replaces relu (choreo-ir.hpp:196-222). */
+int choreo_relu(int32_t dtype, const void* in, void* out, int64_t numel, void* stream);
+
+/* out[i] = a[i] + b[i]. Replaces operator+ (choreo-ir.hpp:150-191). */
+int choreo_add(int32_t dtype, const void* a, const void* b, void* out, int64_t numel,
+               void* stream);
+
+/* dst[i] = value. Replaces the host-vector fill of Tensor::fill
+ * (tensor/tensor.hpp:530-562). */
+int choreo_fill(int32_t dtype, void* dst, double value, int64_t numel, void* stream);
+
+/* dst = convert(src), element count numel (f16/bf16/f32 in any pairing).
+ * Backs the mixed-precision operator* (choreo-ir.hpp:109-145) on the device. */
+int choreo_convert(int32_t dtype_src, const void* src, int32_t dtype_dst, void* dst,
+                   int64_t numel, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CHOREO_B200_H */
