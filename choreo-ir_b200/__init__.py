@@ -74,6 +74,7 @@ _SIGNATURES = {
     "choreo_last_error": (C.c_char_p, []),
     "choreo_device_props_get": (C.c_int, [C.c_int, C.POINTER(DeviceProps)]),
     "choreo_sync_status": (C.c_int, [C.c_void_p]),
+    "choreo_selftest_wait_timeout": (C.c_int, [C.c_double, C.c_void_p]),
     "choreo_gemm_query": (C.c_int, [C.POINTER(GemmDesc), C.POINTER(LaunchConfig)]),
     "choreo_gemm": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p, C.c_size_t, C.c_void_p]),
     "choreo_gemm_rowsharded": (C.c_int, [C.POINTER(GemmDesc), C.c_int, C.POINTER(C.c_int),
@@ -252,6 +253,10 @@ def convert(src, dst, stream=None) -> None:
 
 def sync_status(stream=None) -> None:
     check(lib.choreo_sync_status(_stream_ptr(stream)))
+
+
+def selftest_wait_timeout(timeout_ms: float, stream=None) -> None:
+    check(lib.choreo_selftest_wait_timeout(timeout_ms, _stream_ptr(stream)))
 
 
 def shard_rows(m: int, nshards: int, rank: int) -> tuple[int, int]:

@@ -147,6 +147,15 @@ int choreo_device_props_get(int device, choreo_device_props* out);
  * stream itself reports an error. */
 int choreo_sync_status(void* stream);
 
+/* Launches one CTA that waits, through the bounded wait every kernel
+ * pipeline uses, on an mbarrier nothing arrives on. The wait gives up after
+ * timeout_ms, records a timeout in the status word and the kernel returns:
+ * the next choreo_sync_status() reports CHOREO_ERR_TIMEOUT and the context
+ * stays usable. Exercises the failure path without faulting the GPU. The
+ * reference has no failure detection (errors are host exceptions only,
+ * compute/validation.hpp:20-23, utils/cuda_utils.hpp:26-32). */
+int choreo_selftest_wait_timeout(double timeout_ms, void* stream);
+
 /* ---- GEMM ------------------------------------------------------------- */
 
 /* Validates `d` and reports the kernel configuration and workspace size.
@@ -174,8 +183,9 @@ int choreo_gemm_rowsharded(const choreo_gemm_desc* descs, int ngpu, const int* d
                            void* const* streams, float* ms_out);
 
 /* Rows [*row0, *row0 + *rows) of an M-row problem that shard `rank` of
- * `nshards` owns: contiguous slabs, sizes differing by at most one tile of
- * 128 rows, earlier shards taking the larger slabs. */
+ * `nshards` owns: contiguous slabs of whole 128-row tiles (only the last
+ * slab may end in a partial tile), tile counts differing by at most one,
+ * earlier shards taking the extra tiles. */
 int choreo_shard_rows(int64_t m, int nshards, int rank, int64_t* row0, int64_t* rows);
 
 /* ---- convolution ------------------------------------------------------- */

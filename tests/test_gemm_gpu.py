@@ -1,0 +1,279 @@
+"""GEMM parity on the GPU through the C ABI (libchoreo_b200.so), checked
+against the CPU oracle.
+
+Bar: every output element within 1e-2 relative (floored, see _util.TOL) of
+the fp64 oracle over the same rounded inputs; bit-exact where the inputs make
+the product exact (identity KATs). Against the reference's own CPU path
+(fp16 accumulation) agreement is normwise, and the GPU result must be at
+least as close to fp64 as that path is. Full-size configurations are checked
+on sampled rows (tile boundaries included) plus row/column checksums that
+cover every element.
+"""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from _util import (BF16, F16, F32, TOL, as_f64, assert_close, dev_normal, dev_uniform, sample_rows,
+                   tdtype, to_dev, to_host)
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def run(cb, a, b, m, n, k, dt_ab, dt_c, **kw):
+    import torch
+    c = kw.pop("c", None)
+    if c is None:
+        c = torch.zeros(m, n, device="cuda", dtype=tdtype(dt_c))
+    cb.gemm(a, b, c, **kw)
+    cb.sync_status()
+    return c
+
+
+# ------------------------------------------------------------------ golden fixtures through the GPU
+def test_kat_identity_exact(cb, cuda):
+    g = np.load(GOLDEN / "kat_identity_2x2.npz")
+    for dt, an, bn, cn in ((F16, "a_f16", "b_f16", "c_f16"), (F32, "a_f32", "b_f32", "c_f32")):
+        c = run(cb, to_dev(g[an], dt), to_dev(g[bn], dt), 2, 2, 2, dt, dt)
+        assert np.array_equal(to_host(c), g[cn])
+
+
+def test_kat_wmma_tile(cb, cuda, orc):
+    g = np.load(GOLDEN / "wmma_tile_16.npz")
+    c = run(cb, to_dev(g["a_f16"], F16), to_dev(g["b_f16"], F16), 16, 16, 16, F16, F32)
+    assert np.max(np.abs(to_host(c) - g["c_f32"])) <= float(g["tol"])
+
+
+def test_kat_baselines_f32(cb, cuda):
+    g = np.load(GOLDEN / "baselines_64_f32.npz")
+    c = run(cb, to_dev(g["a"], F32), to_dev(g["b"], F32), 64, 64, 64, F32, F32)
+    assert np.max(np.abs(to_host(c) - g["c"])) <= float(g["tol"])
+
+
+def test_kat_end2end_types(cb, cuda, orc):
+    g = np.load(GOLDEN / "end2end_types_64x32x48.npz")
+    c32 = run(cb, to_dev(g["a_f32"], F32), to_dev(g["b_f32"], F32), 64, 32, 48, F32, F32)
+    assert np.max(np.abs(to_host(c32) - g["c_f32"])) <= 1e-4
+    c16 = to_host(run(cb, to_dev(g["a_f16"], F16), to_dev(g["b_f16"], F16), 64, 32, 48, F16, F16))
+    r64 = orc.gemm_f64(g["a_f16"], g["b_f16"], F16)
+    assert_close(as_f64(c16, F16), r64, what="end2end f16")
+    ref16 = as_f64(g["c_f16"], F16)
+    assert orc.normwise_err(as_f64(c16, F16), ref16) <= TOL
+    assert orc.normwise_err(as_f64(c16, F16), r64) <= orc.normwise_err(ref16, r64) + 1e-12
+
+
+@pytest.mark.parametrize("name", ["ref_matmul_f16_64x48x80.npz", "ref_matmul_bf16_32x24x40.npz",
+                                  "ref_matmul_f32_24x16x40.npz"])
+def test_golden_reference_outputs(cb, cuda, orc, name):
+    g = np.load(GOLDEN / name)
+    dt = int(g["dtype"])
+    (m, k), n = g["a"].shape, g["b"].shape[1]
+    c = to_host(run(cb, to_dev(g["a"], dt), to_dev(g["b"], dt), m, n, k, dt, dt))
+    r64 = orc.gemm_f64(g["a"], g["b"], dt)
+    assert_close(as_f64(c, dt), r64, what=name)
+    ref = as_f64(g["c"], dt)
+    # The reference path accumulates in the input type: bf16 (8-bit mantissa)
+    # drifts a few 1e-2 normwise from fp64 over K = 40, fp16 stays under 1e-2.
+    bar = {F32: 1e-5, F16: TOL, BF16: 4e-2}[dt]
+    assert orc.normwise_err(as_f64(c, dt), ref) <= bar
+    if dt != F32:
+        assert orc.normwise_err(as_f64(c, dt), r64) <= orc.normwise_err(ref, r64)
+
+
+# ------------------------------------------------------------------ config 1: 1024x1024x512 fp16 U[-1,1]
+def test_config1_against_fp64_and_reference_path(cb, cuda, orc):
+    M, N, K = 1024, 1024, 512
+    a = orc.to_bits(orc.uniform((M, K), -1, 1, 42), F16)
+    b = orc.to_bits(orc.uniform((K, N), -1, 1, 43), F16)
+    c = as_f64(to_host(run(cb, to_dev(a, F16), to_dev(b, F16), M, N, K, F16, F16)), F16)
+    r64 = orc.gemm_f64(a, b, F16)
+    assert_close(c, r64, what="config1")
+    ref = as_f64(orc.ref_matmul(a, b, F16, nthreads=orc.threads()), F16)
+    assert orc.normwise_err(c, ref) <= TOL
+    assert orc.normwise_err(c, r64) < orc.normwise_err(ref, r64)
+
+
+# ------------------------------------------------------------------ config 2: square sweep
+@pytest.mark.parametrize("dt", [F16, BF16])
+def test_config2_2048_full(cb, cuda, orc, dt):
+    n = 2048
+    a = orc.to_bits(orc.uniform((n, n), -1, 1, 1), dt)
+    b = orc.to_bits(orc.uniform((n, n), -1, 1, 2), dt)
+    c = as_f64(to_host(run(cb, to_dev(a, dt), to_dev(b, dt), n, n, n, dt, dt)), dt)
+    assert_close(c, orc.gemm_f64(a, b, dt), what=f"2048^3 dt={dt}")
+
+
+@pytest.mark.parametrize("dt", [F16, BF16])
+@pytest.mark.parametrize("n", [4096, 8192])
+def test_config2_large_sampled_and_checksums(cb, cuda, orc, dt, n):
+    import torch
+    a = dev_uniform((n, n), -1, 1, 10 + n, dt)
+    b = dev_uniform((n, n), -1, 1, 20 + n, dt)
+    c = run(cb, a, b, n, n, n, dt, dt)
+    rows = sample_rows(n, 48, seed=n)
+    a_h, b_h = to_host(a[torch.from_numpy(rows).cuda()]), to_host(b)
+    r = orc.gemm_f64(a_h, b_h, dt)
+    assert_close(as_f64(to_host(c[torch.from_numpy(rows).cuda()]), dt), r, what=f"{n}^3 rows")
+    # every element, in aggregate: 1^T C == (1^T A) B and C 1 == A (B 1)
+    c64 = c.double()
+    a64, b64 = a.double(), b.double()
+    col = (a64.sum(0) @ b64)
+    row = (a64 @ b64.sum(1))
+    assert torch.allclose(c64.sum(0), col, rtol=0, atol=2e-3 * float(col.abs().max()) + 1e-6 * n)
+    assert torch.allclose(c64.sum(1), row, rtol=0, atol=2e-3 * float(row.abs().max()) + 1e-6 * n)
+
+
+def test_config2_deterministic(cb, cuda):
+    import torch
+    a = dev_uniform((2048, 2048), -1, 1, 5, F16)
+    b = dev_uniform((2048, 2048), -1, 1, 6, F16)
+    c1 = run(cb, a, b, 2048, 2048, 2048, F16, F16)
+    c2 = run(cb, a, b, 2048, 2048, 2048, F16, F16)
+    assert torch.equal(c1, c2)
+
+
+# ------------------------------------------------------------------ config 3: ragged NN/NT/TN
+@pytest.mark.parametrize("layout", ["NN", "NT", "TN", "TT"])
+def test_config3_ragged_layouts(cb, cuda, orc, layout):
+    import torch
+    M, N, K = 4097, 3000, 1536
+    ta, tb = layout[0] == "T", layout[1] == "T"
+    a = dev_normal((K, M) if ta else (M, K), 0, 1, 31, F16)
+    b = dev_normal((N, K) if tb else (K, N), 0, 1, 32, F16)
+    c = run(cb, a, b, M, N, K, F16, F16, trans_a=ta, trans_b=tb)
+    rows = sample_rows(M, 64, seed=3)
+    r = orc.gemm_f64(to_host(a), to_host(b), F16, trans_a=ta, trans_b=tb, rows=rows)
+    assert_close(as_f64(to_host(c[torch.from_numpy(rows).cuda()]), F16), r, what=f"config3 {layout}")
+    A = a.double().t() if ta else a.double()
+    B = b.double().t() if tb else b.double()
+    col = A.sum(0) @ B
+    assert torch.allclose(c.double().sum(0), col, rtol=0, atol=2e-3 * float(col.abs().max()) + 1e-2)
+
+
+# ------------------------------------------------------------------ config 4: row-sharded 65536x8192x8192 bf16
+def test_config4_full_and_slabs(cb, cuda, orc):
+    import torch
+    M, N, K = 65536, 8192, 8192
+    a = dev_uniform((M, K), -0.5, 0.5, 41, BF16)
+    b = dev_uniform((K, N), -0.5, 0.5, 42, BF16)
+    bias = dev_normal((N,), 0, 0.1, 43, BF16)
+    c = run(cb, a, b, M, N, K, BF16, BF16, bias=bias, relu=True)
+    rows = sample_rows(M, 40, seed=4, tile=8192)
+    r = orc.gemm_f64(to_host(a[torch.from_numpy(rows).cuda()]), to_host(b), BF16, bias=to_host(bias),
+                     dtype_bias=BF16, relu=True)
+    assert_close(as_f64(to_host(c[torch.from_numpy(rows).cuda()]), BF16), r, what="config4 rows")
+    # Each rank's slab computed on its own equals the same rows of the full GEMM.
+    for rank in (0, 3, 7):
+        r0, nrows = cb.shard_rows(M, 8, rank)
+        cs = run(cb, a[r0:r0 + nrows], b, nrows, N, K, BF16, BF16, bias=bias, relu=True)
+        assert torch.equal(cs, c[r0:r0 + nrows])
+    del c
+
+
+# ------------------------------------------------------------------ config 5 lives in test_conv_gpu.py
+
+# ------------------------------------------------------------------ edge cases
+@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (1, 300, 70), (300, 1, 70), (129, 257, 65), (7, 9, 17),
+                                   (128, 256, 64), (255, 136, 8), (64, 8, 4096), (1000, 1000, 1)])
+@pytest.mark.parametrize("dt", [F16, BF16])
+def test_odd_shapes(cb, cuda, orc, m, n, k, dt):
+    a = orc.to_bits(orc.uniform((m, k), -1, 1, m + k), dt)
+    b = orc.to_bits(orc.uniform((k, n), -1, 1, n + k), dt)
+    c = as_f64(to_host(run(cb, to_dev(a, dt), to_dev(b, dt), m, n, k, dt, dt)), dt)
+    assert_close(c, orc.gemm_f64(a, b, dt), what=f"{m}x{n}x{k}")
+
+
+@pytest.mark.parametrize("dt_c", [F16, BF16, F32])
+@pytest.mark.parametrize("dt_bias", [F16, BF16, F32])
+def test_epilogue_alpha_beta_bias_relu(cb, cuda, orc, dt_c, dt_bias):
+    import torch
+    m, n, k = 300, 200, 100
+    a = orc.to_bits(orc.uniform((m, k), -1, 1, 1), BF16)
+    b = orc.to_bits(orc.uniform((k, n), -1, 1, 2), BF16)
+    c0 = orc.uniform((m, n), -1, 1, 3)
+    c0_dev = to_dev(c0, F32).to(tdtype(dt_c))
+    c0_h = to_host(c0_dev)
+    bias = orc.normal((n,), 0, 0.3, 4)
+    bias_dev = to_dev(bias, F32).to(tdtype(dt_bias))
+    c = run(cb, to_dev(a, BF16), to_dev(b, BF16), m, n, k, BF16, dt_c, c=c0_dev.clone(), alpha=0.75, beta=-1.25,
+            bias=bias_dev, relu=True)
+    r = orc.gemm_f64(a, b, BF16, alpha=0.75, beta=-1.25, c0=c0_h, dtype_c0=dt_c, bias=to_host(bias_dev),
+                     dtype_bias=dt_bias, relu=True)
+    assert_close(as_f64(to_host(c), dt_c), r, what="epilogue")
+    assert (to_host(c).astype(np.float64) if dt_c == F32 else as_f64(to_host(c), dt_c)).min() >= 0
+
+
+def test_batched(cb, cuda, orc):
+    import torch
+    batch, m, n, k = 5, 200, 136, 72
+    a = dev_uniform((batch, m, k), -1, 1, 1, F16)
+    b = dev_uniform((batch, k, n), -1, 1, 2, F16)
+    c = torch.zeros(batch, m, n, device="cuda", dtype=torch.float16)
+    cb.gemm(a, b, c)
+    cb.sync_status()
+    for i in range(batch):
+        r = orc.gemm_f64(to_host(a[i]), to_host(b[i]), F16)
+        assert_close(as_f64(to_host(c[i]), F16), r, what=f"batch {i}")
+
+
+def test_padded_leading_dims_use_workspace(cb, cuda, orc):
+    import torch
+    m, n, k = 333, 129, 77
+    a_full = dev_uniform((m, k + 5), -1, 1, 1, F16)
+    b_full = dev_uniform((k, n + 3), -1, 1, 2, F16)
+    a, b = a_full[:, :k], b_full[:, :n]
+    d = cb.make_gemm_desc(a, b, torch.empty(m, n, device="cuda", dtype=torch.float16), m=m, n=n, k=k,
+                          lda=a.stride(0), ldb=b.stride(0))
+    assert cb.gemm_query(d).workspace_bytes > 0
+    with pytest.raises(cb.ChoreoError) as e:
+        cb.gemm_desc(d)
+    assert e.value.code == cb.ERR_WORKSPACE
+    c = run(cb, a, b, m, n, k, F16, F16)
+    r = orc.gemm_f64(to_host(a), to_host(b), F16)
+    assert_close(as_f64(to_host(c), F16), r, what="padded")
+
+
+def test_output_canary(cb, cuda, orc):
+    """C is a window (ldc > N, surrounded by sentinel rows) of a larger buffer:
+    nothing outside the M x N window may change."""
+    import torch
+    m, n, k, ldc = 200, 136, 64, 160
+    buf = torch.full((m + 4, ldc), -7.0, device="cuda", dtype=torch.float16)
+    view = buf[2:2 + m, :n]
+    a = dev_uniform((m, k), -1, 1, 1, F16)
+    b = dev_uniform((k, n), -1, 1, 2, F16)
+    cb.gemm(a, b, view)
+    cb.sync_status()
+    host = buf.float().cpu()
+    assert (host[:2] == -7).all() and (host[2 + m:] == -7).all() and (host[:, n:] == -7).all()
+    r = orc.gemm_f64(to_host(a), to_host(b), F16)
+    assert_close(as_f64(to_host(view), F16), r, what="canary window")
+
+
+def test_host_pointer_rejected(cb, cuda):
+    import torch
+    a = torch.zeros(64, 64, dtype=torch.float16)
+    b = torch.zeros(64, 64, device="cuda", dtype=torch.float16)
+    c = torch.zeros(64, 64, device="cuda", dtype=torch.float16)
+    d = cb.make_gemm_desc(a, b, c, m=64, n=64, k=64)
+    with pytest.raises(cb.ChoreoError) as e:
+        cb.gemm_desc(d)
+    assert e.value.code == cb.ERR_INVALID_ARG and "host memory" in str(e.value)
+
+
+def test_query_reports_tcgen05_config(cb, cuda):
+    import torch
+    x = torch.empty(8192, 8192, device="cuda", dtype=torch.float16)
+    q = cb.gemm_query(cb.make_gemm_desc(x, x, x, m=8192, n=8192, k=8192))
+    assert q.kernel == 1 and q.tile_m == 128 and q.tile_n in (64, 128, 256) and q.block_x == 192
+    assert q.grid_x <= cb.device_props(0).sm_count and q.tmem_cols == 2 * q.tile_n
+    q32 = cb.gemm_query(cb.make_gemm_desc(x.float(), x.float(), x.float(), m=8192, n=8192, k=8192))
+    assert q32.kernel == 2
+
+
+def test_device_props(cb, cuda):
+    p = cb.device_props(0)
+    assert (p.cc_major, p.cc_minor) == (10, 0) and p.sm_count >= 100 and p.max_smem_optin >= 200 * 1024
