@@ -239,12 +239,15 @@ def conv2d_f64(x: np.ndarray, w: np.ndarray, dtype: int, *, stride=1, pad=1, dil
 
 
 # ----------------------------------------------------------------- tolerance
-def rel_err(y: np.ndarray, r: np.ndarray) -> float:
-    """max_i |y - r| / max(|r|, tau), tau = 1e-3 * rms(r): per-element relative
-    error with a floor so outputs that cancel to ~0 do not divide by ~0."""
+def rel_err(y: np.ndarray, r: np.ndarray, k: int | None = None) -> float:
+    """max_i |y - r| / max(|r|, tau): per-element relative error with a floor
+    so outputs that cancel to ~0 do not divide by ~0. tau = 1e-3 * rms(r),
+    widened by sqrt(K / 1024) for reductions longer than 1024 terms, because
+    the absolute error of an fp32 accumulation grows like sqrt(K) * rms."""
     y = np.asarray(y, np.float64)
     r = np.asarray(r, np.float64)
-    tau = 1e-3 * float(np.sqrt(np.mean(r * r))) + 1e-300
+    grow = np.sqrt(max(1.0, (k or 1024) / 1024.0))
+    tau = 1e-3 * grow * float(np.sqrt(np.mean(r * r))) + 1e-300
     return float(np.max(np.abs(y - r) / np.maximum(np.abs(r), tau)))
 
 

@@ -103,7 +103,7 @@ def test_config2_2048_full(cb, cuda, orc, dt):
     a = orc.to_bits(orc.uniform((n, n), -1, 1, 1), dt)
     b = orc.to_bits(orc.uniform((n, n), -1, 1, 2), dt)
     c = as_f64(to_host(run(cb, to_dev(a, dt), to_dev(b, dt), n, n, n, dt, dt)), dt)
-    assert_close(c, orc.gemm_f64(a, b, dt), what=f"2048^3 dt={dt}")
+    assert_close(c, orc.gemm_f64(a, b, dt), what=f"2048^3 dt={dt}", k=n)
 
 
 @pytest.mark.parametrize("dt", [F16, BF16])
@@ -114,9 +114,13 @@ def test_config2_large_sampled_and_checksums(cb, cuda, orc, dt, n):
     b = dev_uniform((n, n), -1, 1, 20 + n, dt)
     c = run(cb, a, b, n, n, n, dt, dt)
     rows = sample_rows(n, 48, seed=n)
-    a_h, b_h = to_host(a[torch.from_numpy(rows).cuda()]), to_host(b)
+    idx = torch.from_numpy(rows).cuda()
+    a_h, b_h = to_host(a[idx]), to_host(b)
     r = orc.gemm_f64(a_h, b_h, dt)
-    assert_close(as_f64(to_host(c[torch.from_numpy(rows).cuda()]), dt), r, what=f"{n}^3 rows")
+    mine = assert_close(as_f64(to_host(c[idx]), dt), r, what=f"{n}^3 rows", k=n)
+    # side reference: cuBLAS (torch.matmul) on the same GPU and rows
+    theirs = orc.rel_err(as_f64(to_host(torch.matmul(a[idx], b)), dt), r, n)
+    assert mine <= max(TOL / 4, 2.0 * theirs), (mine, theirs)
     # every element, in aggregate: 1^T C == (1^T A) B and C 1 == A (B 1)
     c64 = c.double()
     a64, b64 = a.double(), b.double()
@@ -146,7 +150,7 @@ def test_config3_ragged_layouts(cb, cuda, orc, layout):
     c = run(cb, a, b, M, N, K, F16, F16, trans_a=ta, trans_b=tb)
     rows = sample_rows(M, 64, seed=3)
     r = orc.gemm_f64(to_host(a), to_host(b), F16, trans_a=ta, trans_b=tb, rows=rows)
-    assert_close(as_f64(to_host(c[torch.from_numpy(rows).cuda()]), F16), r, what=f"config3 {layout}")
+    assert_close(as_f64(to_host(c[torch.from_numpy(rows).cuda()]), F16), r, what=f"config3 {layout}", k=K)
     A = a.double().t() if ta else a.double()
     B = b.double().t() if tb else b.double()
     col = A.sum(0) @ B
@@ -164,7 +168,7 @@ def test_config4_full_and_slabs(cb, cuda, orc):
     rows = sample_rows(M, 40, seed=4, tile=8192)
     r = orc.gemm_f64(to_host(a[torch.from_numpy(rows).cuda()]), to_host(b), BF16, bias=to_host(bias),
                      dtype_bias=BF16, relu=True)
-    assert_close(as_f64(to_host(c[torch.from_numpy(rows).cuda()]), BF16), r, what="config4 rows")
+    assert_close(as_f64(to_host(c[torch.from_numpy(rows).cuda()]), BF16), r, what="config4 rows", k=K)
     # Each rank's slab computed on its own equals the same rows of the full GEMM.
     for rank in (0, 3, 7):
         r0, nrows = cb.shard_rows(M, 8, rank)
