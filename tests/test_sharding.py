@@ -1,0 +1,123 @@
+"""Row-sharded multi-process logic on CPU: world-size-2 gloo ranks (127.0.0.1).
+
+Each rank takes its slab from choreo_shard_rows (the partition the GPU bench
+uses), computes its rows of C with the fp64 oracle, and rank 0 gathers the
+slabs and compares them with the unsharded result; the timing reduction the
+bench uses (max over ranks) is checked; and a rank that fails before the
+collective makes the other rank's collective raise instead of hanging.
+"""
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, mode: str, out_dir: str) -> None:
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "tests"))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    from conftest import load_choreo
+    from oracle import oracle as orc
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
+    cb = load_choreo()
+    try:
+        if mode == "fail" and rank == 1:
+            raise RuntimeError("injected failure on rank 1 before the collective")
+        M, N, K = 300, 40, 64
+        a = orc.to_bits(orc.uniform((M, K), -0.5, 0.5, 1), orc.BF16)
+        b = orc.to_bits(orc.uniform((K, N), -0.5, 0.5, 2), orc.BF16)
+        bias = orc.normal((N,), 0, 0.1, 3)
+        r0, rows = cb.shard_rows(M, world, rank)
+        slab = orc.gemm_f64(a, b, orc.BF16, bias=bias, dtype_bias=orc.F32, relu=True,
+                            rows=np.arange(r0, r0 + rows), nthreads=1)
+        # gather variable-size slabs: pad to the largest
+        max_rows = (M + 127) // 128 * 128
+        buf = torch.zeros(max_rows, N, dtype=torch.float64)
+        buf[:rows] = torch.from_numpy(slab)
+        meta = torch.tensor([r0, rows], dtype=torch.int64)
+        bufs = [torch.zeros_like(buf) for _ in range(world)]
+        metas = [torch.zeros_like(meta) for _ in range(world)]
+        dist.all_gather(bufs, buf)
+        dist.all_gather(metas, meta)
+        # bench.py's timing reduction: max over ranks
+        t = torch.tensor([10.0 + rank], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        if rank == 0:
+            full = orc.gemm_f64(a, b, orc.BF16, bias=bias, dtype_bias=orc.F32, relu=True, nthreads=1)
+            got = np.zeros_like(full)
+            covered = 0
+            for bb, mm in zip(bufs, metas):
+                s0, n = int(mm[0]), int(mm[1])
+                got[s0:s0 + n] = bb[:n].numpy()
+                covered += n
+            ok = covered == M and np.array_equal(got, full) and float(t[0]) == 10.0 + (world - 1)
+            Path(out_dir, "result").write_text("ok" if ok else "mismatch")
+    except RuntimeError as e:
+        if mode == "fail" and rank == 1:
+            raise
+        Path(out_dir, f"rank{rank}_error").write_text(str(e)[:200])
+        dist.destroy_process_group()
+        sys.exit(3)
+    dist.destroy_process_group()
+
+
+def _spawn(mode: str, tmp_path) -> list[int]:
+    import torch.multiprocessing as mp
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    codes = []
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+            codes.append(-999)
+        else:
+            codes.append(p.exitcode)
+    return codes
+
+
+def test_row_sharded_slabs_assemble_to_full_result(tmp_path):
+    codes = _spawn("ok", tmp_path)
+    assert codes == [0, 0]
+    assert (tmp_path / "result").read_text() == "ok"
+
+
+def test_failed_rank_is_detected_not_hung(tmp_path):
+    codes = _spawn("fail", tmp_path)
+    assert codes[1] != 0                      # the injected failure
+    assert codes[0] == 3                      # rank 0's collective raised and it exited cleanly
+    assert (tmp_path / "rank0_error").exists()
+
+
+def test_bench_workload_specs():
+    sys.path.insert(0, str(ROOT))
+    import bench
+    s = bench.workload_spec("sharded", 8)
+    assert (s["m_total"], s["n"], s["k"], s["dtype"], s["bias"], s["relu"]) == (65536, 8192, 8192, "bf16", True, True)
+    g = bench.workload_spec("gemm8192", 1)
+    assert (g["m_total"], g["n"], g["k"], g["dtype"]) == (8192, 8192, 8192, "f16")
