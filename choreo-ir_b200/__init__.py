@@ -77,6 +77,7 @@ _SIGNATURES = {
     "choreo_selftest_wait_timeout": (C.c_int, [C.c_double, C.c_void_p]),
     "choreo_gemm_query": (C.c_int, [C.POINTER(GemmDesc), C.POINTER(LaunchConfig)]),
     "choreo_gemm": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p, C.c_size_t, C.c_void_p]),
+    "choreo_gemm_noalloc": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p]),
     "choreo_gemm_rowsharded": (C.c_int, [C.POINTER(GemmDesc), C.c_int, C.POINTER(C.c_int),
                                          C.POINTER(C.c_void_p), C.POINTER(C.c_float)]),
     "choreo_shard_rows": (C.c_int, [C.c_int64, C.c_int, C.c_int, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),

@@ -172,6 +172,24 @@ int choreo_gemm_query(const choreo_gemm_desc* d, choreo_launch_config* out);
 int choreo_gemm(const choreo_gemm_desc* d, void* workspace, size_t workspace_bytes,
                 void* stream);
 
+/* Size of the scratch array choreo_gemm_noalloc stages repacked operands in
+ * (one per GPU that loads the library, held until the process exits). */
+#define CHOREO_GEMM_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/* choreo_gemm for callers that cannot allocate device memory: it takes no
+ * workspace and allocates nothing. No counterpart in the reference (its
+ * operator* allocates its output with cudaMalloc, tensor/tensor.hpp:671).
+ * Callers such as plugins inside a runtime that owns all device buffers, or
+ * loops that must not call cudaMalloc (it can synchronize the device and
+ * break a pre-planned memory budget), pass only inputs and outputs; an
+ * operand that needs repacking (not 16-byte aligned) is staged in the
+ * library's built-in scratch array of CHOREO_GEMM_NOALLOC_SCRATCH_BYTES,
+ * and a request needing more returns CHOREO_ERR_WORKSPACE. The first call
+ * on a device resolves the array's address (make it before any stream
+ * capture). All calls on a device share the array: calls that overlap on
+ * the GPU race, so keep them on one stream. */
+int choreo_gemm_noalloc(const choreo_gemm_desc* d, void* stream);
+
 /* Row-sharded GEMM over several GPUs of one process: descs[i] describes
  * device devices[i]'s slab (its own A rows, its replica of B and bias, its C
  * rows). One host thread per device launches on streams[i] (NULL = default
