@@ -54,7 +54,11 @@ def load_choreo():
     return mod
 
 
-def workload_spec(name: str, world: int) -> dict:
+def workload_spec(name: str, world: int, shape: str | None = None, dtype: str = "f16") -> dict:
+    if name == "custom":
+        m, n, k = (int(x) for x in (shape or "4096x4096x4096").lower().split("x"))
+        return dict(workload=f"gemm_{dtype}_{m}x{n}x{k}", m_total=m, n=n, k=k, dtype=dtype,
+                    dist="U[-1,1]", bias=False, relu=False, layout="NN")
     if name == "gemm8192":
         return dict(workload="gemm_f16_8192x8192x8192", m_total=8192, n=8192, k=8192, dtype="f16",
                     dist="U[-1,1]", bias=False, relu=False, layout="NN")
@@ -378,7 +382,11 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="choreo", choices=["choreo", "reference"])
-    ap.add_argument("--workload", default="auto", choices=["auto", "gemm8192", "sharded"])
+    ap.add_argument("--workload", default="auto", choices=["auto", "gemm8192", "sharded", "custom"])
+    ap.add_argument("--shape", default=None, help="MxNxK for --workload custom")
+    ap.add_argument("--dtype", default="f16", choices=["f16", "bf16"], help="input/output type for --workload custom")
+    ap.add_argument("--tile", default=None,
+                    help="force a kernel configuration: pair256, pair128, single256, single128 or single64")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -388,7 +396,9 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     wl = args.workload if args.workload != "auto" else ("gemm8192" if world == 1 else "sharded")
-    spec = workload_spec(wl, world)
+    spec = workload_spec(wl, world, args.shape, args.dtype)
+    if args.tile:
+        os.environ["CHOREO_GEMM_TILE"] = args.tile
 
     if args.impl == "reference":
         bench_reference(args, spec, world, rank)

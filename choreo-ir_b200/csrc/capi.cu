@@ -103,6 +103,27 @@ uint32_t* status_word() {
   return c.status[dev];
 }
 
+L2Plan l2_plan() {
+  // Tiles walk N inside a group of 8 M tiles: the group's A panels are
+  // reused by every later tile of the group, so A is kept in L2 (evict_last);
+  // B k-blocks are shared by the tiles of one wave at about the same time
+  // (evict_normal: evict_first doubles DRAM reads). Measured on the fp16
+  // 8192^3 GEMM: 1.14 GB DRAM read per launch with groups of 8, 1.26 GB
+  // with 16.
+  L2Plan p{1, 0, 8};
+  if (const char* s = std::getenv("CHOREO_L2_POLICY")) {
+    if (s[0] >= '0' && s[0] <= '2' && s[1] >= '0' && s[1] <= '2') {
+      p.policy_a = s[0] - '0';
+      p.policy_b = s[1] - '0';
+    }
+  }
+  if (const char* s = std::getenv("CHOREO_GROUP_M")) {
+    const int g = std::atoi(s);
+    if (g >= 1 && g <= 1024) p.group_m = g;
+  }
+  return p;
+}
+
 uint64_t wait_timeout_ns() {
   static const uint64_t v = [] {
     const char* s = std::getenv("CHOREO_WAIT_TIMEOUT_MS");
@@ -357,14 +378,16 @@ int choreo_gemm_query(const choreo_gemm_desc* d, choreo_launch_config* out) {
     return ok();
   }
   GemmPlan g = plan_tc(*d);
+  const int64_t rows = g.cfg.pair ? 256 : 128;
   out->kernel = 1;
-  out->tile_m = 128;
+  out->tile_m = static_cast<int32_t>(rows);
   out->tile_n = g.cfg.bn;
   out->tile_k = 64;
   out->stages = g.cfg.stages;
-  out->cluster_m = 1;
-  out->tiles = ((d->m + 127) / 128) * ((d->n + g.cfg.bn - 1) / g.cfg.bn) * d->batch;
-  out->grid_x = static_cast<int32_t>(std::min<int64_t>(out->tiles, sms));
+  out->cluster_m = g.cfg.pair ? 2 : 1;
+  out->tiles = ((d->m + rows - 1) / rows) * ((d->n + g.cfg.bn - 1) / g.cfg.bn) * d->batch;
+  out->grid_x = g.cfg.pair ? 2 * static_cast<int32_t>(std::min<int64_t>(out->tiles, sms / 2))
+                           : static_cast<int32_t>(std::min<int64_t>(out->tiles, sms));
   out->grid_y = 1;
   out->grid_z = 1;
   out->block_x = 192;

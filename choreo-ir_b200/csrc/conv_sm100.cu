@@ -25,41 +25,36 @@
 
 namespace choreo_sm100 {
 
-__device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const CUtensorMap* map,
-                                                   uint32_t bar, int32_t c, int32_t w, int32_t h,
-                                                   int32_t n, uint16_t off_w, uint16_t off_h,
-                                                   uint64_t cache_hint) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
-      ".L2::cache_hint [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8}, %9;" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c), "r"(w), "r"(h), "r"(n),
-      "h"(off_w), "h"(off_h), "l"(cache_hint)
-      : "memory");
-}
-
-template <int BN>
+// BNL = output channels one CTA stages per k-block; PAIR selects the
+// CTA-pair TMA form (bytes counted on the pair leader's barrier).
+template <int BNL, bool PAIR>
 struct ConvLoader {
   static constexpr bool kAMn = false;
   static constexpr bool kBMn = false;
   __device__ __forceinline__ static void issue(const CUtensorMap* ta, const CUtensorMap* tb,
-                                               const TcParams& p, int, int mb, int nb, int kb,
+                                               const TcParams& p, int, int m0, int n0, int kb,
                                                uint32_t dst_a, uint32_t dst_b, uint32_t bar,
                                                uint64_t pol_a, uint64_t pol_b) {
     const int rs = kb / p.conv_c_blocks;
     const int cb = kb - rs * p.conv_c_blocks;
     const int r = rs / p.conv_s;
     const int s = rs - r * p.conv_s;
-    const int m0 = mb * kBM;
     const int pq = p.conv_p * p.conv_q;
     const int img = m0 / pq;
     const int rem = m0 - img * pq;
     const int op = rem / p.conv_q;
     const int oq = rem - op * p.conv_q;
-    tma_load_im2col_4d(dst_a, ta, bar, cb * 64, oq * p.conv_stride_w - p.conv_pad_w,
-                       op * p.conv_stride_h - p.conv_pad_h, img,
-                       static_cast<uint16_t>(s * p.conv_dil_w), static_cast<uint16_t>(r * p.conv_dil_h),
-                       pol_a);
-    tma_load_3d(dst_b, tb, bar, cb * 64, rs, nb * BN, pol_b);
+    const int w0 = oq * p.conv_stride_w - p.conv_pad_w;
+    const int h0 = op * p.conv_stride_h - p.conv_pad_h;
+    const uint16_t off_w = static_cast<uint16_t>(s * p.conv_dil_w);
+    const uint16_t off_h = static_cast<uint16_t>(r * p.conv_dil_h);
+    if constexpr (PAIR) {
+      tma_load_im2col_4d_pair(dst_a, ta, bar, cb * 64, w0, h0, img, off_w, off_h, pol_a);
+      tma_load_3d_pair(dst_b, tb, bar, cb * 64, rs, n0, pol_b);
+    } else {
+      tma_load_im2col_4d(dst_a, ta, bar, cb * 64, w0, h0, img, off_w, off_h, pol_a);
+      tma_load_3d(dst_b, tb, bar, cb * 64, rs, n0, pol_b);
+    }
   }
 };
 
@@ -89,32 +84,15 @@ ConvGeom geom(const choreo_conv_desc& d) {
   return g;
 }
 
-int pick_bn(const choreo_conv_desc& d, const ConvGeom& g, int sms) {
-  // Same wave-quantisation model as the GEMM; K <= 64 or 128 caps BN.
-  const int bns[3] = {256, 128, 64};
-  const double eff[3] = {1.0, 0.92, 0.66};
-  const int64_t mt = (g.m + kBM - 1) / kBM;
-  double best = 1e300;
-  int best_bn = 128;
-  for (int i = 0; i < 3; ++i) {
-    const int bn = bns[i];
-    const int64_t nt = (d.k + bn - 1) / bn;
-    const int64_t tiles = mt * nt;
-    const int64_t waves = (tiles + sms - 1) / sms;
-    const double t = static_cast<double>(waves) * (static_cast<double>(g.kblocks) + 4.0) * bn / eff[i];
-    if (t < best * 0.97) { best = t; best_bn = bn; }
-  }
-  return best_bn;
-}
-
 constexpr int conv_stages(int bn) { return bn == 256 ? 4 : (bn == 128 ? 6 : 8); }
+constexpr int conv_pair_stages(int bn) { return bn == 256 ? 7 : 8; }
 
 template <int BN, typename OutT>
 int launch_conv_one(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp, int grid,
                     cudaStream_t stream) {
   constexpr int STAGES = conv_stages(BN);
   constexpr int smem = tc_smem_bytes<BN, STAGES>();
-  auto kern = tc_gemm_kernel<BN, STAGES, ConvLoader<BN>, OutT>;
+  auto kern = tc_gemm_kernel<BN, STAGES, ConvLoader<BN, false>, OutT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(conv)");
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, kp);
@@ -123,46 +101,78 @@ int launch_conv_one(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams
   return CHOREO_OK;
 }
 
+template <int BN, typename OutT>
+int launch_conv_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp, int grid,
+                     cudaStream_t stream) {
+  constexpr int STAGES = conv_pair_stages(BN);
+  constexpr int smem = tc_pair_smem_bytes<BN, STAGES>();
+  auto kern = tc_gemm_pair_kernel<BN, STAGES, ConvLoader<BN / 2, true>, OutT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(conv pair)");
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, kp);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "tcgen05 CTA-pair conv launch");
+  return CHOREO_OK;
+}
+
 template <typename OutT>
-int conv_dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp,
-                     int grid, cudaStream_t s) {
-  switch (bn) {
+int conv_dispatch(const TcConfig& cfg, const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp,
+                  int grid, cudaStream_t s) {
+  if (cfg.pair) {
+    if (cfg.bn == 256) return launch_conv_pair<256, OutT>(ta, tb, kp, grid, s);
+    return launch_conv_pair<128, OutT>(ta, tb, kp, grid, s);
+  }
+  switch (cfg.bn) {
     case 256: return launch_conv_one<256, OutT>(ta, tb, kp, grid, s);
     case 128: return launch_conv_one<128, OutT>(ta, tb, kp, grid, s);
     default: return launch_conv_one<64, OutT>(ta, tb, kp, grid, s);
   }
 }
 
+TcConfig conv_config(const choreo_conv_desc& d, const ConvGeom& g) {
+  TcConfig c = select_tile_config(g.m, d.k, g.kblocks, 1, current_sm_count());
+  if (!c.pair) {
+    c.stages = conv_stages(c.bn);
+  } else {
+    c.stages = conv_pair_stages(c.bn);
+  }
+  return c;
+}
+
+int conv_grid(const TcConfig& c, int64_t tiles) {
+  const int sms = current_sm_count();
+  return c.pair ? 2 * static_cast<int>(std::min<int64_t>(tiles, sms / 2))
+                : static_cast<int>(std::min<int64_t>(tiles, sms));
+}
+
 }  // namespace
 
 int conv_query(const choreo_conv_desc& d, choreo_launch_config* out) {
   const ConvGeom g = geom(d);
-  const int sms = current_sm_count();
-  const int bn = pick_bn(d, g, sms);
+  const TcConfig c = conv_config(d, g);
+  const int64_t rows = c.pair ? 2 * kBM : kBM;
   out->kernel = 3;
-  out->tile_m = kBM;
-  out->tile_n = bn;
+  out->tile_m = static_cast<int32_t>(rows);
+  out->tile_n = c.bn;
   out->tile_k = kBK;
-  out->stages = conv_stages(bn);
-  out->cluster_m = 1;
-  out->tiles = ((g.m + kBM - 1) / kBM) * ((d.k + bn - 1) / bn);
-  out->grid_x = static_cast<int32_t>(std::min<int64_t>(out->tiles, sms));
+  out->stages = c.stages;
+  out->cluster_m = c.pair ? 2 : 1;
+  out->tiles = ((g.m + rows - 1) / rows) * ((d.k + c.bn - 1) / c.bn);
+  out->grid_x = conv_grid(c, out->tiles);
   out->grid_y = 1;
   out->grid_z = 1;
   out->block_x = kThreads;
-  out->smem_bytes = bn == 256 ? tc_smem_bytes<256, conv_stages(256)>()
-                  : bn == 128 ? tc_smem_bytes<128, conv_stages(128)>()
-                              : tc_smem_bytes<64, conv_stages(64)>();
-  out->tmem_cols = 2 * bn;
+  out->smem_bytes = c.smem;
+  out->tmem_cols = 2 * c.bn;
   out->workspace_bytes = 0;
   return CHOREO_OK;
 }
 
 int launch_conv_tc(const choreo_conv_desc& d, cudaStream_t stream) {
   const ConvGeom g = geom(d);
-  choreo_launch_config lc{};
-  conv_query(d, &lc);
-  const int bn = lc.tile_n;
+  const TcConfig cfg = conv_config(d, g);
+  const int bn = cfg.bn;
+  const int64_t tile_rows = cfg.pair ? 2 * kBM : kBM;
   const CUtensorMapDataType tdt = d.dtype == CHOREO_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ta, tb;
@@ -182,7 +192,7 @@ int launch_conv_tc(const choreo_conv_desc& d, cudaStream_t stream) {
     const uint64_t dims[3] = {static_cast<uint64_t>(d.c), static_cast<uint64_t>(d.r * d.s),
                               static_cast<uint64_t>(d.k)};
     const uint64_t strides[2] = {static_cast<uint64_t>(d.c) * 2, static_cast<uint64_t>(d.r * d.s * d.c) * 2};
-    const uint32_t box[3] = {64, 1, static_cast<uint32_t>(bn)};
+    const uint32_t box[3] = {64, 1, static_cast<uint32_t>(cfg.pair ? bn / 2 : bn)};
     int rc = encode_tmap(&tb, tdt, 3, d.weight, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
@@ -190,11 +200,14 @@ int launch_conv_tc(const choreo_conv_desc& d, cudaStream_t stream) {
   kp.m = static_cast<int32_t>(g.m);
   kp.n = static_cast<int32_t>(d.k);
   kp.num_k_blocks = static_cast<int32_t>(g.kblocks);
-  kp.num_m_blocks = static_cast<int32_t>((g.m + kBM - 1) / kBM);
+  kp.num_m_blocks = static_cast<int32_t>((g.m + tile_rows - 1) / tile_rows);
   kp.num_n_blocks = static_cast<int32_t>((d.k + bn - 1) / bn);
   kp.batch = 1;
   kp.num_tiles = static_cast<int64_t>(kp.num_m_blocks) * kp.num_n_blocks;
-  kp.group_m = std::max(1, std::min(16, kp.num_m_blocks));
+  const L2Plan l2 = l2_plan();
+  kp.group_m = std::max(1, std::min(l2.group_m, kp.num_m_blocks));
+  kp.l2_policy_a = l2.policy_a;
+  kp.l2_policy_b = l2.policy_b;
   kp.ab_bf16 = d.dtype == CHOREO_DTYPE_BF16 ? 1 : 0;
   kp.c = d.output;
   kp.ldc = d.k;
@@ -219,11 +232,11 @@ int launch_conv_tc(const choreo_conv_desc& d, cudaStream_t stream) {
   kp.status = status_word();
   kp.timeout_ns = wait_timeout_ns();
   if (kp.status == nullptr) return CHOREO_ERR_CUDA;
-  const int grid = lc.grid_x;
+  const int grid = conv_grid(cfg, kp.num_tiles);
   switch (d.dtype_out) {
-    case CHOREO_DTYPE_F16: return conv_dispatch_bn<__half>(bn, ta, tb, kp, grid, stream);
-    case CHOREO_DTYPE_BF16: return conv_dispatch_bn<__nv_bfloat16>(bn, ta, tb, kp, grid, stream);
-    case CHOREO_DTYPE_F32: return conv_dispatch_bn<float>(bn, ta, tb, kp, grid, stream);
+    case CHOREO_DTYPE_F16: return conv_dispatch<__half>(cfg, ta, tb, kp, grid, stream);
+    case CHOREO_DTYPE_BF16: return conv_dispatch<__nv_bfloat16>(cfg, ta, tb, kp, grid, stream);
+    case CHOREO_DTYPE_F32: return conv_dispatch<float>(cfg, ta, tb, kp, grid, stream);
     default: return fail(CHOREO_ERR_UNSUPPORTED, "conv: unsupported output dtype %d", d.dtype_out);
   }
 }

@@ -13,32 +13,46 @@
 // tile() boundary handling (tensor/layout.hpp:201-209) is realised here.
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 
 #include "internal.h"
 #include "tc_kernel.cuh"
 
 namespace choreo_sm100 {
 
-template <bool A_MN, bool B_MN, int BN>
+// 3-D tiled load through the single-CTA or the CTA-pair form.
+template <bool PAIR>
+__device__ __forceinline__ void load3(uint32_t dst, const CUtensorMap* map, uint32_t bar, int32_t c0, int32_t c1,
+                                      int32_t c2, uint64_t pol) {
+  if constexpr (PAIR)
+    tma_load_3d_pair(dst, map, bar, c0, c1, c2, pol);
+  else
+    tma_load_3d(dst, map, bar, c0, c1, c2, pol);
+}
+
+// BNL = B columns one CTA stages per k-block (the tile's N for a single CTA,
+// half of it for a CTA pair).
+template <bool A_MN, bool B_MN, int BNL, bool PAIR>
 struct GemmLoader {
   static constexpr bool kAMn = A_MN;
   static constexpr bool kBMn = B_MN;
   __device__ __forceinline__ static void issue(const CUtensorMap* ta, const CUtensorMap* tb,
-                                               const TcParams&, int b, int mb, int nb, int kb,
+                                               const TcParams&, int b, int m0, int n0, int kb,
                                                uint32_t dst_a, uint32_t dst_b, uint32_t bar,
                                                uint64_t pol_a, uint64_t pol_b) {
     const int k0 = kb * kBK;
     if constexpr (!A_MN) {
-      tma_load_3d(dst_a, ta, bar, k0, mb * kBM, b, pol_a);
+      load3<PAIR>(dst_a, ta, bar, k0, m0, b, pol_a);
     } else {
-      tma_load_3d(dst_a, ta, bar, mb * kBM, k0, b, pol_a);
-      tma_load_3d(dst_a + 8192, ta, bar, mb * kBM + 64, k0, b, pol_a);
+      load3<PAIR>(dst_a, ta, bar, m0, k0, b, pol_a);
+      load3<PAIR>(dst_a + 8192, ta, bar, m0 + 64, k0, b, pol_a);
     }
     if constexpr (!B_MN) {
-      tma_load_3d(dst_b, tb, bar, k0, nb * BN, b, pol_b);
+      load3<PAIR>(dst_b, tb, bar, k0, n0, b, pol_b);
     } else {
 #pragma unroll
-      for (int j = 0; j < BN / 64; ++j) tma_load_3d(dst_b + j * 8192, tb, bar, nb * BN + j * 64, k0, b, pol_b);
+      for (int j = 0; j < BNL / 64; ++j) load3<PAIR>(dst_b + j * 8192, tb, bar, n0 + j * 64, k0, b, pol_b);
     }
   }
 };
@@ -51,13 +65,14 @@ using namespace choreo_sm100;
 namespace {
 
 constexpr int stages_for(int bn) { return bn == 256 ? 4 : (bn == 128 ? 6 : 8); }
+constexpr int pair_stages_for(int bn) { return bn == 256 ? 7 : 8; }
 
 template <int BN, bool A_MN, bool B_MN, typename OutT>
 int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp, int grid,
                cudaStream_t stream) {
   constexpr int STAGES = stages_for(BN);
   constexpr int smem = tc_smem_bytes<BN, STAGES>();
-  auto kern = tc_gemm_kernel<BN, STAGES, GemmLoader<A_MN, B_MN, BN>, OutT>;
+  auto kern = tc_gemm_kernel<BN, STAGES, GemmLoader<A_MN, B_MN, BN, false>, OutT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, kp);
@@ -66,54 +81,99 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp,
   return CHOREO_OK;
 }
 
-template <int BN, typename OutT>
+template <int BN, bool A_MN, bool B_MN, typename OutT>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp, int grid,
+                cudaStream_t stream) {
+  constexpr int STAGES = pair_stages_for(BN);
+  constexpr int smem = tc_pair_smem_bytes<BN, STAGES>();
+  auto kern = tc_gemm_pair_kernel<BN, STAGES, GemmLoader<A_MN, B_MN, BN / 2, true>, OutT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm pair)");
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, kp);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "tcgen05 CTA-pair GEMM launch");
+  return CHOREO_OK;
+}
+
+template <bool PAIR, int BN, typename OutT>
 int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                    const TcParams& kp, int grid, cudaStream_t s) {
-  if (!a_mn && !b_mn) return launch_one<BN, false, false, OutT>(ta, tb, kp, grid, s);
-  if (!a_mn && b_mn) return launch_one<BN, false, true, OutT>(ta, tb, kp, grid, s);
-  if (a_mn && !b_mn) return launch_one<BN, true, false, OutT>(ta, tb, kp, grid, s);
-  return launch_one<BN, true, true, OutT>(ta, tb, kp, grid, s);
+  if constexpr (PAIR) {
+    if (!a_mn && !b_mn) return launch_pair<BN, false, false, OutT>(ta, tb, kp, grid, s);
+    if (!a_mn && b_mn) return launch_pair<BN, false, true, OutT>(ta, tb, kp, grid, s);
+    if (a_mn && !b_mn) return launch_pair<BN, true, false, OutT>(ta, tb, kp, grid, s);
+    return launch_pair<BN, true, true, OutT>(ta, tb, kp, grid, s);
+  } else {
+    if (!a_mn && !b_mn) return launch_one<BN, false, false, OutT>(ta, tb, kp, grid, s);
+    if (!a_mn && b_mn) return launch_one<BN, false, true, OutT>(ta, tb, kp, grid, s);
+    if (a_mn && !b_mn) return launch_one<BN, true, false, OutT>(ta, tb, kp, grid, s);
+    return launch_one<BN, true, true, OutT>(ta, tb, kp, grid, s);
+  }
 }
 
 template <typename OutT>
-int dispatch_bn(int bn, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+int dispatch_bn(const TcConfig& cfg, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                 const TcParams& kp, int grid, cudaStream_t s) {
-  switch (bn) {
-    case 256: return dispatch_major<256, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
-    case 128: return dispatch_major<128, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
-    default: return dispatch_major<64, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
+  if (cfg.pair) {
+    if (cfg.bn == 256) return dispatch_major<true, 256, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
+    return dispatch_major<true, 128, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
+  }
+  switch (cfg.bn) {
+    case 256: return dispatch_major<false, 256, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
+    case 128: return dispatch_major<false, 128, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
+    default: return dispatch_major<false, 64, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
   }
 }
 
 }  // namespace
 
 TcConfig select_tc_config(int64_t m, int64_t n, int64_t k, int64_t batch, int sm_count) {
-  // Relative cost of one 128-row output tile: a 128 x BN x 16 UMMA reads
-  // (16 KB/4) of A plus BN*32 B of B from shared memory per 128*BN/... cycles;
-  // at BN = 64 shared-memory bandwidth caps the tensor pipe at ~2/3 of peak,
-  // at BN = 128 it is borderline, at 256 it is not limiting.
-  const int bns[3] = {256, 128, 64};
-  const double eff[3] = {1.0, 0.92, 0.66};
-  const int64_t mt = (m + kBM - 1) / kBM;
-  const int64_t kt = (k + kBK - 1) / kBK;
+  return select_tile_config(m, n, (k + kBK - 1) / kBK, batch, sm_count);
+}
+
+TcConfig select_tile_config(int64_t m, int64_t n, int64_t k_blocks, int64_t batch, int sm_count) {
+  // Candidates: CTA pairs (256 x BN tiles on 2 SMs) and single CTAs
+  // (128 x BN). Per SM every candidate computes 128 x BN outputs per tile
+  // step; `eff` is its relative tensor-pipe efficiency (shared-memory operand
+  // bandwidth per MMA and L2 traffic per FLOP favour wide tiles and pairs).
+  // Time ~ waves * (k_blocks + pipeline fill) * BN / eff.
+  struct Cand { bool pair; int bn; double eff; };
+  const Cand cands[5] = {{true, 256, 1.0}, {false, 256, 0.93}, {true, 128, 0.92}, {false, 128, 0.85},
+                         {false, 64, 0.6}};
+  const char* force = std::getenv("CHOREO_GEMM_TILE");  // e.g. "pair256", "single128" (tuning aid)
   double best = 1e300;
-  int best_bn = 256;
-  for (int i = 0; i < 3; ++i) {
-    const int bn = bns[i];
-    const int64_t nt = (n + bn - 1) / bn;
-    const int64_t tiles = mt * nt * batch;
-    const int64_t waves = (tiles + sm_count - 1) / sm_count;
-    // per-tile time ~ (pipeline fill + k blocks) at this tile's efficiency
-    const double per_tile = (static_cast<double>(kt) + 4.0) * bn / eff[i];
-    const double t = static_cast<double>(waves) * per_tile;
-    if (t < best * 0.97) { best = t; best_bn = bn; }
+  TcConfig c{};
+  for (const Cand& cd : cands) {
+    if (force) {
+      char name[32];
+      std::snprintf(name, sizeof(name), "%s%d", cd.pair ? "pair" : "single", cd.bn);
+      if (std::strcmp(force, name) != 0) continue;
+    }
+    const int64_t rows = cd.pair ? 2 * kBM : kBM;
+    const int64_t slots = cd.pair ? sm_count / 2 : sm_count;
+    const int64_t tiles = ((m + rows - 1) / rows) * ((n + cd.bn - 1) / cd.bn) * batch;
+    const int64_t waves = (tiles + slots - 1) / slots;
+    const double t = static_cast<double>(waves) * (static_cast<double>(k_blocks) + 4.0) * cd.bn / cd.eff;
+    if (t < best * 0.97) {
+      best = t;
+      c.pair = cd.pair;
+      c.bn = cd.bn;
+    }
   }
-  TcConfig c;
-  c.bn = best_bn;
-  c.stages = stages_for(best_bn);
-  c.smem = best_bn == 256 ? tc_smem_bytes<256, stages_for(256)>()
-         : best_bn == 128 ? tc_smem_bytes<128, stages_for(128)>()
-                          : tc_smem_bytes<64, stages_for(64)>();
+  if (best == 1e300) {  // unknown forced name: default choice
+    c.pair = true;
+    c.bn = 256;
+  }
+  if (c.pair) {
+    c.stages = pair_stages_for(c.bn);
+    c.smem = c.bn == 256 ? tc_pair_smem_bytes<256, pair_stages_for(256)>()
+                         : tc_pair_smem_bytes<128, pair_stages_for(128)>();
+  } else {
+    c.stages = stages_for(c.bn);
+    c.smem = c.bn == 256 ? tc_smem_bytes<256, stages_for(256)>()
+           : c.bn == 128 ? tc_smem_bytes<128, stages_for(128)>()
+                         : tc_smem_bytes<64, stages_for(64)>();
+  }
   c.group_m = 16;
   return c;
 }
@@ -139,7 +199,8 @@ int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream)
     const uint64_t dims[3] = {inner, outer, static_cast<uint64_t>(p.batch)};
     const uint64_t bstride = p.batch > 1 ? p.stride_b * 2 : outer * p.ldb * 2;
     const uint64_t strides[2] = {static_cast<uint64_t>(p.ldb) * 2, bstride};
-    const uint32_t box[3] = {64, p.b_mn ? 64u : static_cast<uint32_t>(cfg.bn), 1};
+    const uint32_t bnl = static_cast<uint32_t>(cfg.pair ? cfg.bn / 2 : cfg.bn);
+    const uint32_t box[3] = {64, p.b_mn ? 64u : bnl, 1};
     int rc = encode_tmap(&tb, tdt, 3, p.b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
@@ -148,11 +209,15 @@ int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream)
   kp.m = static_cast<int32_t>(p.m);
   kp.n = static_cast<int32_t>(p.n);
   kp.num_k_blocks = static_cast<int32_t>((p.k + kBK - 1) / kBK);
-  kp.num_m_blocks = static_cast<int32_t>((p.m + kBM - 1) / kBM);
+  const int64_t tile_rows = cfg.pair ? 2 * kBM : kBM;
+  kp.num_m_blocks = static_cast<int32_t>((p.m + tile_rows - 1) / tile_rows);
   kp.num_n_blocks = static_cast<int32_t>((p.n + cfg.bn - 1) / cfg.bn);
   kp.batch = static_cast<int32_t>(p.batch);
   kp.num_tiles = static_cast<int64_t>(kp.num_m_blocks) * kp.num_n_blocks * p.batch;
-  kp.group_m = std::max(1, std::min(cfg.group_m, kp.num_m_blocks));
+  const L2Plan l2 = l2_plan();
+  kp.group_m = std::max(1, std::min(l2.group_m, kp.num_m_blocks));
+  kp.l2_policy_a = l2.policy_a;
+  kp.l2_policy_b = l2.policy_b;
   kp.ab_bf16 = p.bf16 ? 1 : 0;
   kp.c = p.c;
   kp.ldc = p.ldc;
@@ -172,12 +237,13 @@ int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream)
   if (kp.status == nullptr) return CHOREO_ERR_CUDA;
 
   const int sms = current_sm_count();
-  const int grid = static_cast<int>(std::min<int64_t>(kp.num_tiles, sms));
+  const int grid = cfg.pair ? 2 * static_cast<int>(std::min<int64_t>(kp.num_tiles, sms / 2))
+                            : static_cast<int>(std::min<int64_t>(kp.num_tiles, sms));
   switch (p.dtype_c) {
-    case CHOREO_DTYPE_F16: return dispatch_bn<__half>(cfg.bn, p.a_mn, p.b_mn, ta, tb, kp, grid, stream);
+    case CHOREO_DTYPE_F16: return dispatch_bn<__half>(cfg, p.a_mn, p.b_mn, ta, tb, kp, grid, stream);
     case CHOREO_DTYPE_BF16:
-      return dispatch_bn<__nv_bfloat16>(cfg.bn, p.a_mn, p.b_mn, ta, tb, kp, grid, stream);
-    case CHOREO_DTYPE_F32: return dispatch_bn<float>(cfg.bn, p.a_mn, p.b_mn, ta, tb, kp, grid, stream);
+      return dispatch_bn<__nv_bfloat16>(cfg, p.a_mn, p.b_mn, ta, tb, kp, grid, stream);
+    case CHOREO_DTYPE_F32: return dispatch_bn<float>(cfg, p.a_mn, p.b_mn, ta, tb, kp, grid, stream);
     default: return fail(CHOREO_ERR_UNSUPPORTED, "unsupported output dtype %d", p.dtype_c);
   }
 }

@@ -32,15 +32,27 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                 CUtensorMapSwizzle swizzle);
 
+// L2 eviction policy codes handed to the kernels (A operand, B operand) and
+// the tile rasterisation group: defaults, overridable for tuning through
+// CHOREO_L2_POLICY="<a><b>" (digits: 0 normal, 1 evict_last, 2 evict_first)
+// and CHOREO_GROUP_M.
+struct L2Plan {
+  int policy_a, policy_b, group_m;
+};
+L2Plan l2_plan();
+
 // ---------------------------------------------------------------- GEMM
 // Tile configurations of the tcgen05 GEMM (BM = 128, BK = 64).
 struct TcConfig {
-  int bn;       // 64, 128 or 256
+  bool pair;    // CTA pair (cluster of 2, tcgen05 cta_group::2): 256-row tiles
+  int bn;       // tile N: 64, 128 or 256 (pairs: 128 or 256)
   int stages;   // shared-memory pipeline depth
-  int smem;     // dynamic shared memory bytes
+  int smem;     // dynamic shared memory bytes per CTA
   int group_m;  // rasterisation group (M tiles walked together for L2 reuse)
 };
 TcConfig select_tc_config(int64_t m, int64_t n, int64_t k, int64_t batch, int sm_count);
+// Same choice from the K-block count (the convolution's K is R*S*ceil(C/64) blocks).
+TcConfig select_tile_config(int64_t m, int64_t n, int64_t k_blocks, int64_t batch, int sm_count);
 
 // A GEMM with every operand already TMA-legal (16-byte aligned base, ld and
 // batch stride), in the orientation it is stored.

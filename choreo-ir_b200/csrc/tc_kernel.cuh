@@ -39,6 +39,7 @@ struct TcParams {
   int64_t num_tiles;
   int32_t group_m;
   int32_t ab_bf16;
+  int32_t l2_policy_a, l2_policy_b;  // 0 evict_normal, 1 evict_last, 2 evict_first
   // epilogue
   void* c;
   int64_t ldc, stride_c;   // elements
@@ -94,6 +95,10 @@ __device__ __forceinline__ float load_bias(const void* bias, int dt, int idx) {
   if (dt == 9) return __ldg(static_cast<const float*>(bias) + idx);
   if (dt == 11) return __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[idx]);
   return __half2float(static_cast<const __half*>(bias)[idx]);
+}
+
+__device__ __forceinline__ uint64_t l2_policy(int code) {
+  return code == 1 ? l2_policy_evict_last() : (code == 2 ? l2_policy_evict_first() : l2_policy_evict_normal());
 }
 
 // Maps a linear tile index to (batch item, M tile, N tile) with grouped
@@ -183,8 +188,10 @@ constexpr int tc_smem_bytes() {
 // Loader contract:
 //   static constexpr bool kAMn, kBMn;          operand majorness in shared memory
 //   __device__ static void issue(const CUtensorMap* ta, const CUtensorMap* tb, const TcParams&,
-//                                int b, int mb, int nb, int kb, uint32_t dst_a, uint32_t dst_b,
+//                                int b, int m0, int n0, int kb, uint32_t dst_a, uint32_t dst_b,
 //                                uint32_t bar, uint64_t pol_a, uint64_t pol_b);
+// loads this CTA's A rows [m0, m0 + 128) and B columns [n0, n0 + B width) for
+// k-block kb of batch item b into the stage at dst_a / dst_b, counted on bar.
 template <int BN, int STAGES, class Loader, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
@@ -233,8 +240,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const uint64_t pol_a = l2_policy_evict_normal();
-      const uint64_t pol_b = l2_policy_evict_last();
+      const uint64_t pol_a = l2_policy(p.l2_policy_a);
+      const uint64_t pol_b = l2_policy(p.l2_policy_b);
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
@@ -247,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t fb = smem_u32(&bars->full[stage]);
           mbar_arrive_expect_tx(fb, kStageBytes);
-          Loader::issue(&tma_a, &tma_b, p, b, mb, nb, kb, smem_u32(s_a + stage * kAStage),
+          Loader::issue(&tma_a, &tma_b, p, b, mb * kBM, nb * BN, kb, smem_u32(s_a + stage * kAStage),
                         smem_u32(s_b + stage * kBStage), fb, pol_a, pol_b);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -344,6 +351,209 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant: a cluster of 2 CTAs on the two SMs of a TPC computes one
+// 256 x BN output tile with tcgen05 cta_group::2 MMAs (M = 256 per
+// instruction). Each CTA stages its own 128 A rows and BN/2 B columns per
+// k-block (A split by M, B split by N across the pair), so a pair moves
+// (256 + BN) x 64 operand elements per k-block for a 256 x BN tile — a third
+// less L2->SM traffic per FLOP than two independent 128 x BN CTAs. Each
+// CTA's TMEM holds its 128 accumulator rows; each CTA's epilogue stores them.
+//   - both producers' TMA loads count their bytes on the LEADER's (rank 0)
+//     full barrier, which the leader's producer arms with both CTAs' bytes;
+//   - the leader's MMA thread releases a stage / publishes an accumulator by
+//     committing to the barrier in each CTA (two plain commits);
+//   - the leader's accumulator-empty barrier takes 8 arrivals: 4 local
+//     epilogue warps and 4 of the peer's (remote mbarrier arrive).
+template <int BN, int STAGES>
+constexpr int tc_pair_smem_bytes() {
+  return STAGES * (kBM * kBK * 2 + (BN / 2) * kBK * 2) + 1024 + static_cast<int>(sizeof(TcBarriers<STAGES>));
+}
+
+template <int BN, int STAGES, class Loader, typename OutT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
+                        const __grid_constant__ CUtensorMap tma_b, const TcParams p) {
+  constexpr int BNL = BN / 2;  // B columns this CTA stages
+  constexpr uint32_t kAStage = kBM * kBK * 2;
+  constexpr uint32_t kBStage = BNL * kBK * 2;
+  constexpr uint32_t kStageBytes = kAStage + kBStage;
+  constexpr uint32_t kTmemCols = 2 * BN;
+  static_assert(BN == 128 || BN == 256, "pair tile N must be 128 or 256");
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* s_a = smem;
+  uint8_t* s_b = smem + STAGES * kAStage;
+  auto* bars = reinterpret_cast<TcBarriers<STAGES>*>(s_b + STAGES * kBStage);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int64_t cluster_id = blockIdx.x >> 1;
+  const int64_t num_clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&bars->full[s]), 1);
+      mbar_init(smem_u32(&bars->empty[s]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&bars->tmem_full[i]), 1);
+      mbar_init(smem_u32(&bars->tmem_empty[i]), 8);
+    }
+    mbar_init(smem_u32(&bars->drain), 1);
+    bars->abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(&bars->tmem_base), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+  const WaitCtx wctx{p.status, p.timeout_ns, &bars->abort};
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producers (both CTAs)
+    if (lane == 0) {
+      const uint64_t pol_a = l2_policy(p.l2_policy_a);
+      const uint64_t pol_b = l2_policy(p.l2_policy_b);
+      uint32_t stage = 0, phase = 0, issued = 0;
+      bool ok = true;
+      for (int64_t t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+        int b, mb, nb;
+        tile_coords(t, p, b, mb, nb);
+        const int m0 = mb * (2 * kBM) + static_cast<int>(rank) * kBM;
+        const int n0 = nb * BN + static_cast<int>(rank) * BNL;
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(&bars->empty[stage]), phase ^ 1, wctx, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t own_full = smem_u32(&bars->full[stage]);
+          if (leader) mbar_arrive_expect_tx(own_full, 2 * kStageBytes);
+          Loader::issue(&tma_a, &tma_b, p, b, m0, n0, kb, smem_u32(s_a + stage * kAStage),
+                        smem_u32(s_b + stage * kBStage), mapa_shared(own_full, 0), pol_a, pol_b);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        if (leader) {
+          const uint32_t inflight = issued < STAGES ? issued : STAGES;
+          uint32_t s = stage, ph = phase;
+          for (uint32_t i = 0; i < inflight; ++i) {
+            if (s == 0) { s = STAGES - 1; ph ^= 1; } else { --s; }
+            mbar_wait(smem_u32(&bars->full[s]), ph, wctx, kStatusTimeoutDrain, false);
+          }
+        } else {
+          // The peer's loads count on the leader's barriers: give them time to land.
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 200000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      const uint32_t idesc = idesc_f16(2 * kBM, BN, p.ab_bf16 != 0, Loader::kAMn, Loader::kBMn);
+      uint32_t stage = 0, phase = 0, local = 0;
+      bool ok = true;
+      for (int64_t t = cluster_id; t < p.num_tiles && ok; t += num_clusters, ++local) {
+        const uint32_t buf = local & 1;
+        const uint32_t tph = (local >> 1) & 1;
+        if (!mbar_wait(smem_u32(&bars->tmem_empty[buf]), tph ^ 1, wctx, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(&bars->full[stage]), phase, wctx, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(s_a + stage * kAStage);
+          const uint32_t b0 = smem_u32(s_b + stage * kBStage);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = Loader::kAMn ? smem_desc_sw128(a0 + k * 2048, 8192, 1024)
+                                             : smem_desc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bd = Loader::kBMn ? smem_desc_sw128(b0 + k * 2048, 8192, 1024)
+                                             : smem_desc_sw128(b0 + k * 32, 16, 1024);
+            umma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          const uint32_t eb = smem_u32(&bars->empty[stage]);
+          umma_commit_pair(eb);
+          umma_commit_pair(mapa_shared(eb, 1));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        const uint32_t fb = smem_u32(&bars->tmem_full[buf]);
+        umma_commit_pair(fb);
+        umma_commit_pair(mapa_shared(fb, 1));
+      }
+      umma_commit_pair(smem_u32(&bars->drain));
+      mbar_wait(smem_u32(&bars->drain), 0, wctx, kStatusTimeoutDrain, false);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;
+    uint32_t local = 0;
+    for (int64_t t = cluster_id; t < p.num_tiles; t += num_clusters, ++local) {
+      const uint32_t buf = local & 1;
+      const uint32_t tph = (local >> 1) & 1;
+      int ready = 0;
+      if (lane == 0)
+        ready = mbar_wait(smem_u32(&bars->tmem_full[buf]), tph, wctx, kStatusTimeoutEpilogue) ? 1 : 0;
+      ready = __shfl_sync(0xffffffffu, ready, 0);
+      if (!ready) break;
+      tc_fence_after();
+      int b, mb, nb;
+      tile_coords(t, p, b, mb, nb);
+      const int row = mb * (2 * kBM) + static_cast<int>(rank) * kBM + quarter * 32 + lane;
+      const bool row_ok = row < p.m;
+      OutT* crow = static_cast<OutT*>(p.c) + static_cast<int64_t>(b) * p.stride_c +
+                   static_cast<int64_t>(row_ok ? row : 0) * p.ldc;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int n_base = nb * BN + c * 32;
+        if (n_base >= p.n) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        tmem_wait_ld();
+        epilogue_chunk<OutT>(r, crow, n_base, p, row_ok);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        const uint32_t eb = smem_u32(&bars->tmem_empty[buf]);
+        if (leader)
+          mbar_arrive(eb);
+        else
+          mbar_arrive_cluster(mapa_shared(eb, 0));
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // both CTAs done (MMAs drained, epilogues finished) before TMEM is freed
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 

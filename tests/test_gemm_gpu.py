@@ -272,7 +272,8 @@ def test_query_reports_tcgen05_config(cb, cuda):
     import torch
     x = torch.empty(8192, 8192, device="cuda", dtype=torch.float16)
     q = cb.gemm_query(cb.make_gemm_desc(x, x, x, m=8192, n=8192, k=8192))
-    assert q.kernel == 1 and q.tile_m == 128 and q.tile_n in (64, 128, 256) and q.block_x == 192
+    assert q.kernel == 1 and q.tile_n in (64, 128, 256) and q.block_x == 192
+    assert (q.tile_m, q.cluster_m) in ((128, 1), (256, 2))
     assert q.grid_x <= cb.device_props(0).sm_count and q.tmem_cols == 2 * q.tile_n
     q32 = cb.gemm_query(cb.make_gemm_desc(x.float(), x.float(), x.float(), m=8192, n=8192, k=8192))
     assert q32.kernel == 2
@@ -281,3 +282,33 @@ def test_query_reports_tcgen05_config(cb, cuda):
 def test_device_props(cb, cuda):
     p = cb.device_props(0)
     assert (p.cc_major, p.cc_minor) == (10, 0) and p.sm_count >= 100 and p.max_smem_optin >= 200 * 1024
+
+
+# ------------------------------------------------------------------ every tile configuration
+TILES = ["pair256", "pair128", "single256", "single128", "single64"]
+
+
+@pytest.fixture
+def force_tile(monkeypatch):
+    def _set(name):
+        monkeypatch.setenv("CHOREO_GEMM_TILE", name)
+    return _set
+
+
+@pytest.mark.parametrize("tile", TILES)
+@pytest.mark.parametrize("layout", ["NN", "NT", "TN", "TT"])
+@pytest.mark.parametrize("m,n,k", [(517, 390, 200), (1024, 768, 1000)])
+def test_forced_tile_configs(cb, cuda, orc, force_tile, tile, layout, m, n, k):
+    import torch
+    force_tile(tile)
+    ta, tb = layout[0] == "T", layout[1] == "T"
+    a = dev_uniform((k, m) if ta else (m, k), -1, 1, m + k, BF16)
+    b = dev_uniform((n, k) if tb else (k, n), -1, 1, n + k, BF16)
+    bias = dev_normal((n,), 0, 0.2, 3, F32)
+    c = run(cb, a, b, m, n, k, BF16, BF16, trans_a=ta, trans_b=tb, bias=bias, relu=True)
+    desc = cb.make_gemm_desc(a, b, c, m=m, n=n, k=k, trans_a=ta, trans_b=tb, lda=a.stride(0), ldb=b.stride(0))
+    q = cb.gemm_query(desc)
+    assert (q.tile_m, q.tile_n, q.cluster_m) == ((256, int(tile[4:]), 2) if tile.startswith("pair")
+                                                   else (128, int(tile[6:]), 1))
+    r = orc.gemm_f64(to_host(a), to_host(b), BF16, trans_a=ta, trans_b=tb, bias=to_host(bias), relu=True)
+    assert_close(as_f64(to_host(c), BF16), r, what=f"{tile} {layout} {m}x{n}x{k}", k=k)
