@@ -104,13 +104,13 @@ uint32_t* status_word() {
 }
 
 L2Plan l2_plan() {
-  // Tiles walk N inside a group of 8 M tiles: the group's A panels are
-  // reused by every later tile of the group, so A is kept in L2 (evict_last);
-  // B k-blocks are shared by the tiles of one wave at about the same time
-  // (evict_normal: evict_first doubles DRAM reads). Measured on the fp16
-  // 8192^3 GEMM: 1.14 GB DRAM read per launch with groups of 8, 1.26 GB
-  // with 16.
-  L2Plan p{1, 0, 8};
+  // Tiles walk N inside a group of M tiles covering 2048 rows: the group's A
+  // panels are reused by every later tile of the group, so A is kept in L2
+  // (evict_last); B k-blocks are shared by the tiles of one wave at about the
+  // same time (evict_normal: evict_first doubles DRAM reads). Measured on the
+  // fp16 8192^3 GEMM with 256-row tiles: 1.14 GB DRAM read per launch with
+  // 2048-row groups, 1.26 GB with 4096.
+  L2Plan p{1, 0, 2048, 0};
   if (const char* s = std::getenv("CHOREO_L2_POLICY")) {
     if (s[0] >= '0' && s[0] <= '2' && s[1] >= '0' && s[1] <= '2') {
       p.policy_a = s[0] - '0';
@@ -378,7 +378,7 @@ int choreo_gemm_query(const choreo_gemm_desc* d, choreo_launch_config* out) {
     return ok();
   }
   GemmPlan g = plan_tc(*d);
-  const int64_t rows = g.cfg.pair ? 256 : 128;
+  const int64_t rows = tile_rows_of(g.cfg);
   out->kernel = 1;
   out->tile_m = static_cast<int32_t>(rows);
   out->tile_n = g.cfg.bn;

@@ -19,6 +19,7 @@
 // benchmark/kernels/gemm_example.cu:208-253 (direct conv with stride and
 // zero padding, KCRS weights, NCHW), restated for NHWC/KRSC.
 #include <algorithm>
+#include <cstring>
 
 #include "internal.h"
 #include "tc_kernel.cuh"
@@ -31,10 +32,9 @@ template <int BNL, bool PAIR>
 struct ConvLoader {
   static constexpr bool kAMn = false;
   static constexpr bool kBMn = false;
-  __device__ __forceinline__ static void issue(const CUtensorMap* ta, const CUtensorMap* tb,
-                                               const TcParams& p, int, int m0, int n0, int kb,
-                                               uint32_t dst_a, uint32_t dst_b, uint32_t bar,
-                                               uint64_t pol_a, uint64_t pol_b) {
+  // 128 output pixels starting at pixel m0 (NHW order) for k-block kb = (r, s, channel block).
+  __device__ __forceinline__ static void issue_a(const CUtensorMap* ta, const TcParams& p, int, int m0, int kb,
+                                                 uint32_t dst_a, uint32_t bar, uint64_t pol_a) {
     const int rs = kb / p.conv_c_blocks;
     const int cb = kb - rs * p.conv_c_blocks;
     const int r = rs / p.conv_s;
@@ -48,13 +48,27 @@ struct ConvLoader {
     const int h0 = op * p.conv_stride_h - p.conv_pad_h;
     const uint16_t off_w = static_cast<uint16_t>(s * p.conv_dil_w);
     const uint16_t off_h = static_cast<uint16_t>(r * p.conv_dil_h);
-    if constexpr (PAIR) {
+    if constexpr (PAIR)
       tma_load_im2col_4d_pair(dst_a, ta, bar, cb * 64, w0, h0, img, off_w, off_h, pol_a);
-      tma_load_3d_pair(dst_b, tb, bar, cb * 64, rs, n0, pol_b);
-    } else {
+    else
       tma_load_im2col_4d(dst_a, ta, bar, cb * 64, w0, h0, img, off_w, off_h, pol_a);
+  }
+  // Output channels [n0, n0 + BNL) of the weights for k-block kb.
+  __device__ __forceinline__ static void issue_b(const CUtensorMap* tb, const TcParams& p, int, int n0, int kb,
+                                                 uint32_t dst_b, uint32_t bar, uint64_t pol_b) {
+    const int rs = kb / p.conv_c_blocks;
+    const int cb = kb - rs * p.conv_c_blocks;
+    if constexpr (PAIR)
+      tma_load_3d_pair(dst_b, tb, bar, cb * 64, rs, n0, pol_b);
+    else
       tma_load_3d(dst_b, tb, bar, cb * 64, rs, n0, pol_b);
-    }
+  }
+  __device__ __forceinline__ static void issue(const CUtensorMap* ta, const CUtensorMap* tb,
+                                               const TcParams& p, int b, int m0, int n0, int kb,
+                                               uint32_t dst_a, uint32_t dst_b, uint32_t bar,
+                                               uint64_t pol_a, uint64_t pol_b) {
+    issue_a(ta, p, b, m0, kb, dst_a, bar, pol_a);
+    issue_b(tb, p, b, n0, kb, dst_b, bar, pol_b);
   }
 };
 
@@ -86,6 +100,20 @@ ConvGeom geom(const choreo_conv_desc& d) {
 
 constexpr int conv_stages(int bn) { return bn == 256 ? 4 : (bn == 128 ? 6 : 8); }
 constexpr int conv_pair_stages(int bn) { return bn == 256 ? 7 : 8; }
+constexpr int kConvWideStages = 4;
+
+template <typename OutT>
+int launch_conv_wide(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& kp,
+                     int grid, cudaStream_t stream) {
+  constexpr int smem = tc_wide_smem_bytes<kConvWideStages>();
+  auto kern = tc_gemm_pair_wide_kernel<kConvWideStages, ConvLoader<128, true>, OutT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(conv wide)");
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "tcgen05 wide CTA-pair conv launch");
+  return CHOREO_OK;
+}
 
 template <int BN, typename OutT>
 int launch_conv_one(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp, int grid,
@@ -116,8 +144,9 @@ int launch_conv_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcParam
 }
 
 template <typename OutT>
-int conv_dispatch(const TcConfig& cfg, const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp,
-                  int grid, cudaStream_t s) {
+int conv_dispatch(const TcConfig& cfg, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                  const TcParams& kp, int grid, cudaStream_t s) {
+  if (cfg.wide) return launch_conv_wide<OutT>(ta, tb, tc, kp, grid, s);
   if (cfg.pair) {
     if (cfg.bn == 256) return launch_conv_pair<256, OutT>(ta, tb, kp, grid, s);
     return launch_conv_pair<128, OutT>(ta, tb, kp, grid, s);
@@ -131,11 +160,7 @@ int conv_dispatch(const TcConfig& cfg, const CUtensorMap& ta, const CUtensorMap&
 
 TcConfig conv_config(const choreo_conv_desc& d, const ConvGeom& g) {
   TcConfig c = select_tile_config(g.m, d.k, g.kblocks, 1, current_sm_count());
-  if (!c.pair) {
-    c.stages = conv_stages(c.bn);
-  } else {
-    c.stages = conv_pair_stages(c.bn);
-  }
+  c.stages = c.wide ? kConvWideStages : (c.pair ? conv_pair_stages(c.bn) : conv_stages(c.bn));
   return c;
 }
 
@@ -150,7 +175,7 @@ int conv_grid(const TcConfig& c, int64_t tiles) {
 int conv_query(const choreo_conv_desc& d, choreo_launch_config* out) {
   const ConvGeom g = geom(d);
   const TcConfig c = conv_config(d, g);
-  const int64_t rows = c.pair ? 2 * kBM : kBM;
+  const int64_t rows = tile_rows_of(c);
   out->kernel = 3;
   out->tile_m = static_cast<int32_t>(rows);
   out->tile_n = c.bn;
@@ -172,7 +197,7 @@ int launch_conv_tc(const choreo_conv_desc& d, cudaStream_t stream) {
   const ConvGeom g = geom(d);
   const TcConfig cfg = conv_config(d, g);
   const int bn = cfg.bn;
-  const int64_t tile_rows = cfg.pair ? 2 * kBM : kBM;
+  const int64_t tile_rows = tile_rows_of(cfg);
   const CUtensorMapDataType tdt = d.dtype == CHOREO_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ta, tb;
@@ -205,7 +230,7 @@ int launch_conv_tc(const choreo_conv_desc& d, cudaStream_t stream) {
   kp.batch = 1;
   kp.num_tiles = static_cast<int64_t>(kp.num_m_blocks) * kp.num_n_blocks;
   const L2Plan l2 = l2_plan();
-  kp.group_m = std::max(1, std::min(l2.group_m, kp.num_m_blocks));
+  kp.group_m = group_tiles(l2, static_cast<int>(tile_rows), kp.num_m_blocks);
   kp.l2_policy_a = l2.policy_a;
   kp.l2_policy_b = l2.policy_b;
   kp.ab_bf16 = d.dtype == CHOREO_DTYPE_BF16 ? 1 : 0;
@@ -216,6 +241,21 @@ int launch_conv_tc(const choreo_conv_desc& d, cudaStream_t stream) {
   kp.c_vec_ok = ((reinterpret_cast<uintptr_t>(d.output) & 15u) == 0 && (d.k * ob) % 16 == 0) ? 1 : 0;
   kp.alpha = d.alpha;
   kp.beta = 0.f;
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof(tc));
+  kp.c_tma = 0;
+  if (cfg.wide && kp.c_vec_ok) {
+    const uint64_t elem = static_cast<uint64_t>(ob);
+    const uint64_t dims[3] = {static_cast<uint64_t>(d.k), static_cast<uint64_t>(g.m), 1};
+    const uint64_t strides[2] = {static_cast<uint64_t>(d.k) * elem, static_cast<uint64_t>(g.m) * d.k * elem};
+    const uint32_t box[3] = {static_cast<uint32_t>(128 / elem), 32, 1};
+    const CUtensorMapDataType cdt = d.dtype_out == CHOREO_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                  : d.dtype_out == CHOREO_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    int rc = encode_tmap(&tc, cdt, 3, d.output, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    kp.c_tma = 1;
+  }
   kp.bias = d.bias;
   kp.dtype_bias = d.dtype_bias;
   kp.relu = d.relu;
@@ -234,9 +274,9 @@ int launch_conv_tc(const choreo_conv_desc& d, cudaStream_t stream) {
   if (kp.status == nullptr) return CHOREO_ERR_CUDA;
   const int grid = conv_grid(cfg, kp.num_tiles);
   switch (d.dtype_out) {
-    case CHOREO_DTYPE_F16: return conv_dispatch<__half>(cfg, ta, tb, kp, grid, stream);
-    case CHOREO_DTYPE_BF16: return conv_dispatch<__nv_bfloat16>(cfg, ta, tb, kp, grid, stream);
-    case CHOREO_DTYPE_F32: return conv_dispatch<float>(cfg, ta, tb, kp, grid, stream);
+    case CHOREO_DTYPE_F16: return conv_dispatch<__half>(cfg, ta, tb, tc, kp, grid, stream);
+    case CHOREO_DTYPE_BF16: return conv_dispatch<__nv_bfloat16>(cfg, ta, tb, tc, kp, grid, stream);
+    case CHOREO_DTYPE_F32: return conv_dispatch<float>(cfg, ta, tb, tc, kp, grid, stream);
     default: return fail(CHOREO_ERR_UNSUPPORTED, "conv: unsupported output dtype %d", d.dtype_out);
   }
 }

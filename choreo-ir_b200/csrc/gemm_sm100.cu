@@ -37,10 +37,9 @@ template <bool A_MN, bool B_MN, int BNL, bool PAIR>
 struct GemmLoader {
   static constexpr bool kAMn = A_MN;
   static constexpr bool kBMn = B_MN;
-  __device__ __forceinline__ static void issue(const CUtensorMap* ta, const CUtensorMap* tb,
-                                               const TcParams&, int b, int m0, int n0, int kb,
-                                               uint32_t dst_a, uint32_t dst_b, uint32_t bar,
-                                               uint64_t pol_a, uint64_t pol_b) {
+  // A rows [m0, m0 + 128) of k-block kb.
+  __device__ __forceinline__ static void issue_a(const CUtensorMap* ta, const TcParams&, int b, int m0, int kb,
+                                                 uint32_t dst_a, uint32_t bar, uint64_t pol_a) {
     const int k0 = kb * kBK;
     if constexpr (!A_MN) {
       load3<PAIR>(dst_a, ta, bar, k0, m0, b, pol_a);
@@ -48,12 +47,24 @@ struct GemmLoader {
       load3<PAIR>(dst_a, ta, bar, m0, k0, b, pol_a);
       load3<PAIR>(dst_a + 8192, ta, bar, m0 + 64, k0, b, pol_a);
     }
+  }
+  // B columns [n0, n0 + BNL) of k-block kb.
+  __device__ __forceinline__ static void issue_b(const CUtensorMap* tb, const TcParams&, int b, int n0, int kb,
+                                                 uint32_t dst_b, uint32_t bar, uint64_t pol_b) {
+    const int k0 = kb * kBK;
     if constexpr (!B_MN) {
       load3<PAIR>(dst_b, tb, bar, k0, n0, b, pol_b);
     } else {
 #pragma unroll
       for (int j = 0; j < BNL / 64; ++j) load3<PAIR>(dst_b + j * 8192, tb, bar, n0 + j * 64, k0, b, pol_b);
     }
+  }
+  __device__ __forceinline__ static void issue(const CUtensorMap* ta, const CUtensorMap* tb,
+                                               const TcParams& p, int b, int m0, int n0, int kb,
+                                               uint32_t dst_a, uint32_t dst_b, uint32_t bar,
+                                               uint64_t pol_a, uint64_t pol_b) {
+    issue_a(ta, p, b, m0, kb, dst_a, bar, pol_a);
+    issue_b(tb, p, b, n0, kb, dst_b, bar, pol_b);
   }
 };
 
@@ -66,6 +77,7 @@ namespace {
 
 constexpr int stages_for(int bn) { return bn == 256 ? 4 : (bn == 128 ? 6 : 8); }
 constexpr int pair_stages_for(int bn) { return bn == 256 ? 7 : 8; }
+constexpr int kWideStages = 4;
 
 template <int BN, bool A_MN, bool B_MN, typename OutT>
 int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp, int grid,
@@ -95,6 +107,28 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp
   return CHOREO_OK;
 }
 
+template <bool A_MN, bool B_MN, typename OutT>
+int launch_wide(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& kp,
+                int grid, cudaStream_t stream) {
+  constexpr int smem = tc_wide_smem_bytes<kWideStages>();
+  auto kern = tc_gemm_pair_wide_kernel<kWideStages, GemmLoader<A_MN, B_MN, 128, true>, OutT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm wide)");
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "tcgen05 wide CTA-pair GEMM launch");
+  return CHOREO_OK;
+}
+
+template <typename OutT>
+int dispatch_wide(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                  const TcParams& kp, int grid, cudaStream_t s) {
+  if (!a_mn && !b_mn) return launch_wide<false, false, OutT>(ta, tb, tc, kp, grid, s);
+  if (!a_mn && b_mn) return launch_wide<false, true, OutT>(ta, tb, tc, kp, grid, s);
+  if (a_mn && !b_mn) return launch_wide<true, false, OutT>(ta, tb, tc, kp, grid, s);
+  return launch_wide<true, true, OutT>(ta, tb, tc, kp, grid, s);
+}
+
 template <bool PAIR, int BN, typename OutT>
 int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                    const TcParams& kp, int grid, cudaStream_t s) {
@@ -113,7 +147,8 @@ int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMa
 
 template <typename OutT>
 int dispatch_bn(const TcConfig& cfg, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                const TcParams& kp, int grid, cudaStream_t s) {
+                const CUtensorMap& tc, const TcParams& kp, int grid, cudaStream_t s) {
+  if (cfg.wide) return dispatch_wide<OutT>(a_mn, b_mn, ta, tb, tc, kp, grid, s);
   if (cfg.pair) {
     if (cfg.bn == 256) return dispatch_major<true, 256, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
     return dispatch_major<true, 128, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
@@ -132,39 +167,45 @@ TcConfig select_tc_config(int64_t m, int64_t n, int64_t k, int64_t batch, int sm
 }
 
 TcConfig select_tile_config(int64_t m, int64_t n, int64_t k_blocks, int64_t batch, int sm_count) {
-  // Candidates: CTA pairs (256 x BN tiles on 2 SMs) and single CTAs
-  // (128 x BN). Per SM every candidate computes 128 x BN outputs per tile
-  // step; `eff` is its relative tensor-pipe efficiency (shared-memory operand
-  // bandwidth per MMA and L2 traffic per FLOP favour wide tiles and pairs).
-  // Time ~ waves * (k_blocks + pipeline fill) * BN / eff.
-  struct Cand { bool pair; int bn; double eff; };
-  const Cand cands[5] = {{true, 256, 1.0}, {false, 256, 0.93}, {true, 128, 0.92}, {false, 128, 0.85},
-                         {false, 64, 0.6}};
-  const char* force = std::getenv("CHOREO_GEMM_TILE");  // e.g. "pair256", "single128" (tuning aid)
+  // Candidates: wide CTA pairs (512 x 256 tiles on 2 SMs), CTA pairs
+  // (256 x BN) and single CTAs (128 x BN). Per SM a tile step computes
+  // rows_per_sm x BN outputs; `eff` is the candidate's relative tensor-pipe
+  // efficiency (shared-memory operand bandwidth per MMA and L2 traffic per
+  // FLOP favour wide tiles and pairs) and `fixed` its per-tile overhead in
+  // k-blocks (pipeline fill; for the wide tile, the half of the epilogue
+  // that is not overlapped). Time ~ waves * (k_blocks + fixed) * rows_per_sm * BN / eff.
+  struct Cand { const char* name; bool pair, wide; int bn; double eff, fixed; };
+  const Cand cands[6] = {{"wide256", true, true, 256, 1.10, 6.0},  {"pair256", true, false, 256, 1.0, 4.0},
+                         {"single256", false, false, 256, 0.97, 4.0}, {"pair128", true, false, 128, 0.92, 4.0},
+                         {"single128", false, false, 128, 0.85, 4.0}, {"single64", false, false, 64, 0.6, 4.0}};
+  const char* force = std::getenv("CHOREO_GEMM_TILE");  // e.g. "wide256", "single128" (tuning aid)
   double best = 1e300;
   TcConfig c{};
   for (const Cand& cd : cands) {
-    if (force) {
-      char name[32];
-      std::snprintf(name, sizeof(name), "%s%d", cd.pair ? "pair" : "single", cd.bn);
-      if (std::strcmp(force, name) != 0) continue;
-    }
-    const int64_t rows = cd.pair ? 2 * kBM : kBM;
+    if (force && std::strcmp(force, cd.name) != 0) continue;
+    const int64_t rows = cd.wide ? 4 * kBM : (cd.pair ? 2 * kBM : kBM);
+    const int64_t rows_per_sm = cd.wide ? 2 * kBM : kBM;
     const int64_t slots = cd.pair ? sm_count / 2 : sm_count;
     const int64_t tiles = ((m + rows - 1) / rows) * ((n + cd.bn - 1) / cd.bn) * batch;
     const int64_t waves = (tiles + slots - 1) / slots;
-    const double t = static_cast<double>(waves) * (static_cast<double>(k_blocks) + 4.0) * cd.bn / cd.eff;
+    const double t = static_cast<double>(waves) * (static_cast<double>(k_blocks) + cd.fixed) *
+                     static_cast<double>(rows_per_sm * cd.bn) / cd.eff;
     if (t < best * 0.97) {
       best = t;
       c.pair = cd.pair;
+      c.wide = cd.wide;
       c.bn = cd.bn;
     }
   }
   if (best == 1e300) {  // unknown forced name: default choice
     c.pair = true;
+    c.wide = false;
     c.bn = 256;
   }
-  if (c.pair) {
+  if (c.wide) {
+    c.stages = kWideStages;
+    c.smem = tc_wide_smem_bytes<kWideStages>();
+  } else if (c.pair) {
     c.stages = pair_stages_for(c.bn);
     c.smem = c.bn == 256 ? tc_pair_smem_bytes<256, pair_stages_for(256)>()
                          : tc_pair_smem_bytes<128, pair_stages_for(128)>();
@@ -174,7 +215,7 @@ TcConfig select_tile_config(int64_t m, int64_t n, int64_t k_blocks, int64_t batc
            : c.bn == 128 ? tc_smem_bytes<128, stages_for(128)>()
                          : tc_smem_bytes<64, stages_for(64)>();
   }
-  c.group_m = 16;
+  c.group_m = 0;
   return c;
 }
 
@@ -209,13 +250,13 @@ int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream)
   kp.m = static_cast<int32_t>(p.m);
   kp.n = static_cast<int32_t>(p.n);
   kp.num_k_blocks = static_cast<int32_t>((p.k + kBK - 1) / kBK);
-  const int64_t tile_rows = cfg.pair ? 2 * kBM : kBM;
+  const int64_t tile_rows = tile_rows_of(cfg);
   kp.num_m_blocks = static_cast<int32_t>((p.m + tile_rows - 1) / tile_rows);
   kp.num_n_blocks = static_cast<int32_t>((p.n + cfg.bn - 1) / cfg.bn);
   kp.batch = static_cast<int32_t>(p.batch);
   kp.num_tiles = static_cast<int64_t>(kp.num_m_blocks) * kp.num_n_blocks * p.batch;
   const L2Plan l2 = l2_plan();
-  kp.group_m = std::max(1, std::min(l2.group_m, kp.num_m_blocks));
+  kp.group_m = group_tiles(l2, static_cast<int>(tile_rows), kp.num_m_blocks);
   kp.l2_policy_a = l2.policy_a;
   kp.l2_policy_b = l2.policy_b;
   kp.ab_bf16 = p.bf16 ? 1 : 0;
@@ -232,6 +273,25 @@ int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream)
   kp.bias = p.bias;
   kp.dtype_bias = p.dtype_bias;
   kp.relu = p.relu;
+  // The wide kernel stores C through a staging tile and a TMA store when C is
+  // TMA-addressable (16-byte aligned base, leading dimension and batch stride).
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof(tc));
+  kp.c_tma = 0;
+  if (cfg.wide && kp.c_vec_ok) {
+    const uint64_t elem = static_cast<uint64_t>(cb);
+    const uint64_t dims[3] = {static_cast<uint64_t>(p.n), static_cast<uint64_t>(p.m), static_cast<uint64_t>(p.batch)};
+    const uint64_t bstride = p.batch > 1 ? static_cast<uint64_t>(p.stride_c) * elem
+                                         : static_cast<uint64_t>(p.m) * static_cast<uint64_t>(p.ldc) * elem;
+    const uint64_t strides[2] = {static_cast<uint64_t>(p.ldc) * elem, bstride};
+    const uint32_t box[3] = {static_cast<uint32_t>(128 / elem), 32, 1};
+    const CUtensorMapDataType cdt = p.dtype_c == CHOREO_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                  : p.dtype_c == CHOREO_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    int rc = encode_tmap(&tc, cdt, 3, p.c, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    kp.c_tma = 1;
+  }
   kp.status = status_word();
   kp.timeout_ns = wait_timeout_ns();
   if (kp.status == nullptr) return CHOREO_ERR_CUDA;
@@ -240,10 +300,10 @@ int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream)
   const int grid = cfg.pair ? 2 * static_cast<int>(std::min<int64_t>(kp.num_tiles, sms / 2))
                             : static_cast<int>(std::min<int64_t>(kp.num_tiles, sms));
   switch (p.dtype_c) {
-    case CHOREO_DTYPE_F16: return dispatch_bn<__half>(cfg, p.a_mn, p.b_mn, ta, tb, kp, grid, stream);
+    case CHOREO_DTYPE_F16: return dispatch_bn<__half>(cfg, p.a_mn, p.b_mn, ta, tb, tc, kp, grid, stream);
     case CHOREO_DTYPE_BF16:
-      return dispatch_bn<__nv_bfloat16>(cfg, p.a_mn, p.b_mn, ta, tb, kp, grid, stream);
-    case CHOREO_DTYPE_F32: return dispatch_bn<float>(cfg, p.a_mn, p.b_mn, ta, tb, kp, grid, stream);
+      return dispatch_bn<__nv_bfloat16>(cfg, p.a_mn, p.b_mn, ta, tb, tc, kp, grid, stream);
+    case CHOREO_DTYPE_F32: return dispatch_bn<float>(cfg, p.a_mn, p.b_mn, ta, tb, tc, kp, grid, stream);
     default: return fail(CHOREO_ERR_UNSUPPORTED, "unsupported output dtype %d", p.dtype_c);
   }
 }

@@ -37,20 +37,30 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
 // CHOREO_L2_POLICY="<a><b>" (digits: 0 normal, 1 evict_last, 2 evict_first)
 // and CHOREO_GROUP_M.
 struct L2Plan {
-  int policy_a, policy_b, group_m;
+  int policy_a, policy_b;
+  int group_rows;   // rows of A walked together (group = group_rows / tile rows M tiles)
+  int group_m;      // > 0: explicit group in M tiles (tuning override)
 };
+inline int group_tiles(const L2Plan& p, int tile_rows, int num_m_blocks) {
+  int g = p.group_m > 0 ? p.group_m : p.group_rows / tile_rows;
+  if (g < 1) g = 1;
+  return g < num_m_blocks ? g : num_m_blocks;
+}
+
 L2Plan l2_plan();
 
 // ---------------------------------------------------------------- GEMM
 // Tile configurations of the tcgen05 GEMM (BM = 128, BK = 64).
 struct TcConfig {
   bool pair;    // CTA pair (cluster of 2, tcgen05 cta_group::2): 256-row tiles
-  int bn;       // tile N: 64, 128 or 256 (pairs: 128 or 256)
+  bool wide;    // CTA pair with two M halves per CTA: 512 x 256 tiles
+  int bn;       // tile N: 64, 128 or 256 (pairs: 128 or 256; wide: 256)
   int stages;   // shared-memory pipeline depth
   int smem;     // dynamic shared memory bytes per CTA
   int group_m;  // rasterisation group (M tiles walked together for L2 reuse)
 };
 TcConfig select_tc_config(int64_t m, int64_t n, int64_t k, int64_t batch, int sm_count);
+inline int tile_rows_of(const TcConfig& c) { return c.wide ? 512 : (c.pair ? 256 : 128); }
 // Same choice from the K-block count (the convolution's K is R*S*ceil(C/64) blocks).
 TcConfig select_tile_config(int64_t m, int64_t n, int64_t k_blocks, int64_t batch, int sm_count);
 

@@ -44,6 +44,7 @@ struct TcParams {
   void* c;
   int64_t ldc, stride_c;   // elements
   int32_t c_vec_ok;        // 16-byte vector stores are legal for C
+  int32_t c_tma;           // C is TMA-addressable: the wide kernel stores through a staging tile
   float alpha, beta;
   const void* bias;
   int32_t dtype_bias;      // 8 f16, 9 f32, 11 bf16
@@ -116,11 +117,10 @@ __device__ __forceinline__ void tile_coords(int64_t t, const TcParams& p, int& b
   nb = in / gm;
 }
 
-// Epilogue for one 32-column chunk of one row held by this thread.
+// alpha * acc + beta * C + bias, then ReLU, for one 32-column chunk of one row.
 template <typename OutT>
-__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], OutT* crow, int n_base,
-                                               const TcParams& p, bool row_ok) {
-  float v[32];
+__device__ __forceinline__ void epilogue_values(const uint32_t (&r)[32], float (&v)[32], const OutT* crow,
+                                                int n_base, const TcParams& p, bool row_ok) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
   const bool full = (n_base + 32 <= p.n);
@@ -138,6 +138,43 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], OutT* cr
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = (v[i] < 0.f) ? 0.f : v[i];  // NaN passes, like std::max(x, 0)
   }
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+// Writes 32 converted values of this thread's row into a 128-byte-swizzled
+// staging row (the layout a SWIZZLE_128B TMA store reads), starting at
+// 16-byte chunk `chunk0` of the row. Lanes 8 apart share a chunk position, so
+// each 8-lane phase of the warp's stores hits 32 distinct banks.
+template <typename OutT>
+__device__ __forceinline__ void stage_row_32(const float (&v)[32], uint32_t row_addr, int lane, int chunk0) {
+  const int sw = lane & 7;
+  if constexpr (sizeof(OutT) == 2) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      st_shared_v4(row_addr + (((chunk0 + j) ^ sw) << 4), pack2(v[8 * j + 0], v[8 * j + 1], static_cast<OutT*>(nullptr)),
+                   pack2(v[8 * j + 2], v[8 * j + 3], static_cast<OutT*>(nullptr)),
+                   pack2(v[8 * j + 4], v[8 * j + 5], static_cast<OutT*>(nullptr)),
+                   pack2(v[8 * j + 6], v[8 * j + 7], static_cast<OutT*>(nullptr)));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      st_shared_v4(row_addr + (((chunk0 + j) ^ sw) << 4), __float_as_uint(v[4 * j + 0]), __float_as_uint(v[4 * j + 1]),
+                   __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
+  }
+}
+
+// Epilogue for one 32-column chunk of one row held by this thread (direct
+// global stores: 16-byte vectors where legal, scalars at ragged edges).
+template <typename OutT>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], OutT* crow, int n_base,
+                                               const TcParams& p, bool row_ok) {
+  float v[32];
+  epilogue_values<OutT>(r, v, crow, n_base, p, row_ok);
+  const bool full = (n_base + 32 <= p.n);
   if (!row_ok) return;
   if constexpr (sizeof(OutT) == 2) {
     if (full && p.c_vec_ok) {
@@ -551,6 +588,267 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   cluster_sync();  // both CTAs done (MMAs drained, epilogues finished) before TMEM is freed
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Wide CTA-pair variant: the pair computes a 512 x 256 tile as two M = 256
+// halves that share every B k-block (two cta_group::2 MMAs per k-step). Each
+// CTA stages 2 x 128 A rows and 128 B columns per k-block and keeps a
+// 256 x 256 fp32 accumulator (its 128 rows of each half) in all 512 TMEM
+// columns: a quarter less L2 -> SM operand traffic per FLOP than 256 x 256
+// tiles. With no room for a second accumulator, overlap comes from draining
+// the accumulator in halves: the epilogue releases half 0 as soon as it has
+// read it, and the next tile's first k-block issues its half-0 MMAs while the
+// epilogue is still reading half 1.
+template <int STAGES>
+struct alignas(8) TcWideBarriers {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full;      // this tile's accumulator is complete (leader commit, count 1)
+  uint64_t tmem_empty[2];  // accumulator half h drained by the pair's 8 epilogue warps (leader's, count 8)
+  uint64_t drain;
+  uint32_t tmem_base;
+  int32_t abort;
+};
+
+// Epilogue staging: 4 warps x 2 buffers x (32 rows x 128 bytes).
+constexpr int kStagingBytes = 4 * 2 * 4096;
+
+template <int STAGES>
+constexpr int tc_wide_smem_bytes() {
+  return STAGES * (2 * kBM * kBK * 2 + 128 * kBK * 2) + kStagingBytes + 1024 +
+         static_cast<int>(sizeof(TcWideBarriers<STAGES>));
+}
+
+template <int STAGES, class Loader, typename OutT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    tc_gemm_pair_wide_kernel(const __grid_constant__ CUtensorMap tma_a,
+                             const __grid_constant__ CUtensorMap tma_b,
+                             const __grid_constant__ CUtensorMap tma_c, const TcParams p) {
+  constexpr int BN = 256;
+  constexpr int BNL = 128;
+  constexpr uint32_t kAHalf = kBM * kBK * 2;   // 128 rows x 64 (16 KB)
+  constexpr uint32_t kAStage = 2 * kAHalf;
+  constexpr uint32_t kBStage = BNL * kBK * 2;  // 16 KB
+  constexpr uint32_t kStageBytes = kAStage + kBStage;
+  constexpr uint32_t kTmemCols = 512;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* s_a = smem;
+  uint8_t* s_b = smem + STAGES * kAStage;
+  uint8_t* s_stage = s_b + STAGES * kBStage;  // 1024-aligned: every stage is a multiple of 1 KB
+  auto* bars = reinterpret_cast<TcWideBarriers<STAGES>*>(s_stage + kStagingBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int64_t cluster_id = blockIdx.x >> 1;
+  const int64_t num_clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&bars->full[s]), 1);
+      mbar_init(smem_u32(&bars->empty[s]), 1);
+    }
+    if (p.c_tma) tma_prefetch_desc(&tma_c);
+    mbar_init(smem_u32(&bars->tmem_full), 1);
+    mbar_init(smem_u32(&bars->tmem_empty[0]), 8);
+    mbar_init(smem_u32(&bars->tmem_empty[1]), 8);
+    mbar_init(smem_u32(&bars->drain), 1);
+    bars->abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(&bars->tmem_base), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+  const WaitCtx wctx{p.status, p.timeout_ns, &bars->abort};
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producers (both CTAs)
+    if (lane == 0) {
+      const uint64_t pol_a = l2_policy(p.l2_policy_a);
+      const uint64_t pol_b = l2_policy(p.l2_policy_b);
+      uint32_t stage = 0, phase = 0, issued = 0;
+      bool ok = true;
+      for (int64_t t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+        int b, mb, nb;
+        tile_coords(t, p, b, mb, nb);
+        const int m0 = mb * (4 * kBM) + static_cast<int>(rank) * kBM;
+        const int n0 = nb * BN + static_cast<int>(rank) * BNL;
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(&bars->empty[stage]), phase ^ 1, wctx, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t own_full = smem_u32(&bars->full[stage]);
+          if (leader) mbar_arrive_expect_tx(own_full, 2 * kStageBytes);
+          const uint32_t bar = mapa_shared(own_full, 0);
+          const uint32_t a_dst = smem_u32(s_a + stage * kAStage);
+          Loader::issue_a(&tma_a, p, b, m0, kb, a_dst, bar, pol_a);
+          Loader::issue_a(&tma_a, p, b, m0 + 2 * kBM, kb, a_dst + kAHalf, bar, pol_a);
+          Loader::issue_b(&tma_b, p, b, n0, kb, smem_u32(s_b + stage * kBStage), bar, pol_b);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        if (leader) {
+          const uint32_t inflight = issued < STAGES ? issued : STAGES;
+          uint32_t s = stage, ph = phase;
+          for (uint32_t i = 0; i < inflight; ++i) {
+            if (s == 0) { s = STAGES - 1; ph ^= 1; } else { --s; }
+            mbar_wait(smem_u32(&bars->full[s]), ph, wctx, kStatusTimeoutDrain, false);
+          }
+        } else {
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 200000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      const uint32_t idesc = idesc_f16(2 * kBM, BN, p.ab_bf16 != 0, Loader::kAMn, Loader::kBMn);
+      uint32_t stage = 0, phase = 0, local = 0;
+      bool ok = true;
+      for (int64_t t = cluster_id; t < p.num_tiles && ok; t += num_clusters, ++local) {
+        const uint32_t tph = local & 1;
+        for (int kb = 0; kb < p.num_k_blocks && ok; ++kb) {
+          if (!mbar_wait(smem_u32(&bars->full[stage]), phase, wctx, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(s_a + stage * kAStage);
+          const uint32_t b0 = smem_u32(s_b + stage * kBStage);
+          for (int h = 0; h < 2; ++h) {
+            if (kb == 0) {
+              // this half of the accumulator must have been read out by the previous tile's epilogue
+              if (!mbar_wait(smem_u32(&bars->tmem_empty[h]), tph ^ 1, wctx, kStatusTimeoutMma)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            const uint32_t ah = a0 + h * kAHalf;
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+              const uint64_t ad = Loader::kAMn ? smem_desc_sw128(ah + k * 2048, 8192, 1024)
+                                               : smem_desc_sw128(ah + k * 32, 16, 1024);
+              const uint64_t bd = Loader::kBMn ? smem_desc_sw128(b0 + k * 2048, 8192, 1024)
+                                               : smem_desc_sw128(b0 + k * 32, 16, 1024);
+              umma_f16_pair(tmem_base + h * BN, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
+          }
+          if (!ok) break;
+          const uint32_t eb = smem_u32(&bars->empty[stage]);
+          umma_commit_pair(eb);
+          umma_commit_pair(mapa_shared(eb, 1));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        const uint32_t fb = smem_u32(&bars->tmem_full);
+        umma_commit_pair(fb);
+        umma_commit_pair(mapa_shared(fb, 1));
+      }
+      umma_commit_pair(smem_u32(&bars->drain));
+      mbar_wait(smem_u32(&bars->drain), 0, wctx, kStatusTimeoutDrain, false);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;
+    constexpr int E = 128 / static_cast<int>(sizeof(OutT));  // columns per 128-byte staging row
+    const uint32_t stage_base = smem_u32(s_stage) + static_cast<uint32_t>(warp - 2) * 8192u;
+    uint32_t store_iter = 0;
+    uint32_t local = 0;
+    for (int64_t t = cluster_id; t < p.num_tiles; t += num_clusters, ++local) {
+      int ready = 0;
+      if (lane == 0)
+        ready = mbar_wait(smem_u32(&bars->tmem_full), local & 1, wctx, kStatusTimeoutEpilogue) ? 1 : 0;
+      ready = __shfl_sync(0xffffffffu, ready, 0);
+      if (!ready) break;
+      tc_fence_after();
+      int b, mb, nb;
+      tile_coords(t, p, b, mb, nb);
+      for (int h = 0; h < 2; ++h) {
+        const int row0 = mb * (4 * kBM) + h * (2 * kBM) + static_cast<int>(rank) * kBM + quarter * 32;
+        const int row = row0 + lane;
+        const bool row_ok = row < p.m;
+        OutT* crow = static_cast<OutT*>(p.c) + static_cast<int64_t>(b) * p.stride_c +
+                     static_cast<int64_t>(row_ok ? row : 0) * p.ldc;
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + h * BN;
+        if (p.c_tma) {
+          // TMEM -> registers -> swizzled staging tile -> bulk tensor store (clipped at the edges).
+          if (row0 < p.m) {  // warp-uniform
+#pragma unroll 1
+            for (int g = 0; g < BN / E; ++g) {
+              const int n_base = nb * BN + g * E;
+              if (n_base >= p.n) break;  // warp-uniform
+              const uint32_t buf = stage_base + (store_iter & 1u) * 4096u;
+              if (lane == 0) bulk_wait_read_le1();  // the store issued two groups ago has read this buffer
+              __syncwarp();
+#pragma unroll
+              for (int c = 0; c < E / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(taddr + g * E + c * 32, r);
+                tmem_wait_ld();
+                float v[32];
+                epilogue_values<OutT>(r, v, crow, n_base + c * 32, p, row_ok);
+                stage_row_32<OutT>(v, buf + static_cast<uint32_t>(lane) * 128u, lane,
+                                   c * (32 * static_cast<int>(sizeof(OutT)) / 16));
+              }
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_3d(&tma_c, buf, n_base, row0, b);
+                bulk_commit_group();
+              }
+              ++store_iter;
+            }
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            const int n_base = nb * BN + c * 32;
+            if (n_base >= p.n) break;  // warp-uniform
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(taddr + c * 32, r);
+            tmem_wait_ld();
+            epilogue_chunk<OutT>(r, crow, n_base, p, row_ok);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          const uint32_t eb = smem_u32(&bars->tmem_empty[h]);
+          if (leader)
+            mbar_arrive(eb);
+          else
+            mbar_arrive_cluster(mapa_shared(eb, 0));
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_all();  // staged stores finished before the CTA's shared memory goes away
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  cluster_sync();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols);

@@ -94,11 +94,11 @@ def test_conv_query(cb, cuda):
     o = torch.empty(32, 56, 56, 256, device="cuda", dtype=torch.float16)
     q = cb.conv2d_query(cb.conv_desc(x, w, o))
     assert q.kernel == 3 and q.workspace_bytes == 0
-    assert (q.tile_m, q.cluster_m) in ((128, 1), (256, 2))
-    assert q.tiles == (32 * 56 * 56 // q.tile_m) * (256 // q.tile_n)
+    assert (q.tile_m, q.cluster_m) in ((128, 1), (256, 2), (512, 2))
+    assert q.tiles == -(-32 * 56 * 56 // q.tile_m) * (256 // q.tile_n)
 
 
-@pytest.mark.parametrize("tile", ["pair256", "pair128", "single256", "single128", "single64"])
+@pytest.mark.parametrize("tile", ["wide256", "pair256", "pair128", "single256", "single128", "single64"])
 def test_conv_forced_tiles(cb, cuda, orc, monkeypatch, tile):
     monkeypatch.setenv("CHOREO_GEMM_TILE", tile)
     x = orc.to_bits(orc.uniform((3, 13, 11, 128), 0, 1, 7), F16)
@@ -106,6 +106,6 @@ def test_conv_forced_tiles(cb, cuda, orc, monkeypatch, tile):
     bias = orc.normal((192,), 0, 0.1, 9)
     out = run_conv(cb, to_dev(x, F16), to_dev(wt, F16), F16, bias=to_dev(bias, F32), relu=True)
     q = cb.conv2d_query(cb.conv_desc(to_dev(x, F16), to_dev(wt, F16), out))
-    assert q.cluster_m == (2 if tile.startswith("pair") else 1)
+    assert q.cluster_m == (2 if tile.startswith(("pair", "wide")) else 1)
     ref = orc.conv2d_f64(x, wt, F16, bias=bias, dtype_bias=F32, relu=True)
     assert_close(as_f64(to_host(out), F16).reshape(-1, 192), ref, what=f"conv {tile}", k=9 * 128)

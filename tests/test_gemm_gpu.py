@@ -273,7 +273,7 @@ def test_query_reports_tcgen05_config(cb, cuda):
     x = torch.empty(8192, 8192, device="cuda", dtype=torch.float16)
     q = cb.gemm_query(cb.make_gemm_desc(x, x, x, m=8192, n=8192, k=8192))
     assert q.kernel == 1 and q.tile_n in (64, 128, 256) and q.block_x == 192
-    assert (q.tile_m, q.cluster_m) in ((128, 1), (256, 2))
+    assert (q.tile_m, q.cluster_m) in ((128, 1), (256, 2), (512, 2))
     assert q.grid_x <= cb.device_props(0).sm_count and q.tmem_cols == 2 * q.tile_n
     q32 = cb.gemm_query(cb.make_gemm_desc(x.float(), x.float(), x.float(), m=8192, n=8192, k=8192))
     assert q32.kernel == 2
@@ -285,7 +285,7 @@ def test_device_props(cb, cuda):
 
 
 # ------------------------------------------------------------------ every tile configuration
-TILES = ["pair256", "pair128", "single256", "single128", "single64"]
+TILES = ["wide256", "pair256", "pair128", "single256", "single128", "single64"]
 
 
 @pytest.fixture
@@ -297,7 +297,7 @@ def force_tile(monkeypatch):
 
 @pytest.mark.parametrize("tile", TILES)
 @pytest.mark.parametrize("layout", ["NN", "NT", "TN", "TT"])
-@pytest.mark.parametrize("m,n,k", [(517, 390, 200), (1024, 768, 1000)])
+@pytest.mark.parametrize("m,n,k", [(517, 390, 200), (1024, 768, 1000), (777, 392, 130)])
 def test_forced_tile_configs(cb, cuda, orc, force_tile, tile, layout, m, n, k):
     import torch
     force_tile(tile)
@@ -308,7 +308,39 @@ def test_forced_tile_configs(cb, cuda, orc, force_tile, tile, layout, m, n, k):
     c = run(cb, a, b, m, n, k, BF16, BF16, trans_a=ta, trans_b=tb, bias=bias, relu=True)
     desc = cb.make_gemm_desc(a, b, c, m=m, n=n, k=k, trans_a=ta, trans_b=tb, lda=a.stride(0), ldb=b.stride(0))
     q = cb.gemm_query(desc)
-    assert (q.tile_m, q.tile_n, q.cluster_m) == ((256, int(tile[4:]), 2) if tile.startswith("pair")
-                                                   else (128, int(tile[6:]), 1))
+    want = {"wide256": (512, 256, 2), "pair256": (256, 256, 2), "pair128": (256, 128, 2),
+            "single256": (128, 256, 1), "single128": (128, 128, 1), "single64": (128, 64, 1)}[tile]
+    assert (q.tile_m, q.tile_n, q.cluster_m) == want
     r = orc.gemm_f64(to_host(a), to_host(b), BF16, trans_a=ta, trans_b=tb, bias=to_host(bias), relu=True)
     assert_close(as_f64(to_host(c), BF16), r, what=f"{tile} {layout} {m}x{n}x{k}", k=k)
+
+
+@pytest.mark.parametrize("tile", ["wide256", "pair256", "single128"])
+@pytest.mark.parametrize("dt_c", [F16, F32])
+def test_forced_tile_canary_and_batch(cb, cuda, orc, force_tile, tile, dt_c):
+    """Staged (TMA-store) and direct epilogues write exactly the M x N window of
+    a larger buffer, for single and batched problems."""
+    import torch
+    force_tile(tile)
+    m, n, k, ldc = 600, 264, 96, 320
+    buf = torch.full((m + 8, ldc), -7.0, device="cuda", dtype=tdtype(dt_c))
+    view = buf[3:3 + m, :n]
+    a = dev_uniform((m, k), -1, 1, 11, F16)
+    b = dev_uniform((k, n), -1, 1, 12, F16)
+    cb.gemm(a, b, view)
+    cb.sync_status()
+    host = buf.float().cpu()
+    assert (host[:3] == -7).all() and (host[3 + m:] == -7).all() and (host[:, n:] == -7).all()
+    r = orc.gemm_f64(to_host(a), to_host(b), F16)
+    got = to_host(view).astype(np.float64) if dt_c == F32 else as_f64(to_host(view), dt_c)
+    assert_close(got, r, what=f"canary {tile}")
+    batch = 3
+    ab = dev_uniform((batch, m, k), -1, 1, 13, F16)
+    bb = dev_uniform((batch, k, n), -1, 1, 14, F16)
+    cbt = torch.zeros(batch, m, n, device="cuda", dtype=tdtype(dt_c))
+    cb.gemm(ab, bb, cbt)
+    cb.sync_status()
+    for i in range(batch):
+        r = orc.gemm_f64(to_host(ab[i]), to_host(bb[i]), F16)
+        got = to_host(cbt[i]).astype(np.float64) if dt_c == F32 else as_f64(to_host(cbt[i]), dt_c)
+        assert_close(got, r, what=f"batch {i} {tile}")
