@@ -724,41 +724,70 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (leader && lane == 0) {
       const uint32_t idesc = idesc_f16(2 * kBM, BN, p.ab_bf16 != 0, Loader::kAMn, Loader::kBMn);
+      // The MMAs of one accumulator half for one stage.
+      auto issue_half = [&](int h, uint32_t st, int kb) {
+        const uint32_t ah = smem_u32(s_a + st * kAStage) + h * kAHalf;
+        const uint32_t b0 = smem_u32(s_b + st * kBStage);
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {
+          const uint64_t ad = Loader::kAMn ? smem_desc_sw128(ah + k * 2048, 8192, 1024)
+                                           : smem_desc_sw128(ah + k * 32, 16, 1024);
+          const uint64_t bd = Loader::kBMn ? smem_desc_sw128(b0 + k * 2048, 8192, 1024)
+                                           : smem_desc_sw128(b0 + k * 32, 16, 1024);
+          umma_f16_pair(tmem_base + h * BN, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+        }
+      };
+      auto release = [&](uint32_t st) {
+        const uint32_t eb = smem_u32(&bars->empty[st]);
+        umma_commit_pair(eb);
+        umma_commit_pair(mapa_shared(eb, 1));
+      };
       uint32_t stage = 0, phase = 0, local = 0;
       bool ok = true;
       for (int64_t t = cluster_id; t < p.num_tiles && ok; t += num_clusters, ++local) {
         const uint32_t tph = local & 1;
-        for (int kb = 0; kb < p.num_k_blocks && ok; ++kb) {
+        // Head of the tile: the first D stages (already prefetched while the
+        // previous tile's epilogue ran) are consumed for half 0 as soon as the
+        // epilogue has read half 0 out, and replayed for half 1 (then
+        // released) once it has read half 1 — the half-1 drain overlaps
+        // D k-blocks of half-0 MMAs.
+        const int D = p.num_k_blocks < STAGES ? p.num_k_blocks : STAGES;
+        if (!mbar_wait(smem_u32(&bars->tmem_empty[0]), tph ^ 1, wctx, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t st = stage, ph = phase;
+        for (int kb = 0; kb < D; ++kb) {
+          if (!mbar_wait(smem_u32(&bars->full[st]), ph, wctx, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_half(0, st, kb);
+          if (++st == STAGES) { st = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        if (!mbar_wait(smem_u32(&bars->tmem_empty[1]), tph ^ 1, wctx, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < D; ++kb) {
+          issue_half(1, stage, kb);
+          release(stage);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        // Steady state: both halves per stage.
+        for (int kb = D; kb < p.num_k_blocks; ++kb) {
           if (!mbar_wait(smem_u32(&bars->full[stage]), phase, wctx, kStatusTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(s_a + stage * kAStage);
-          const uint32_t b0 = smem_u32(s_b + stage * kBStage);
-          for (int h = 0; h < 2; ++h) {
-            if (kb == 0) {
-              // this half of the accumulator must have been read out by the previous tile's epilogue
-              if (!mbar_wait(smem_u32(&bars->tmem_empty[h]), tph ^ 1, wctx, kStatusTimeoutMma)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-            }
-            const uint32_t ah = a0 + h * kAHalf;
-#pragma unroll
-            for (int k = 0; k < kBK / 16; ++k) {
-              const uint64_t ad = Loader::kAMn ? smem_desc_sw128(ah + k * 2048, 8192, 1024)
-                                               : smem_desc_sw128(ah + k * 32, 16, 1024);
-              const uint64_t bd = Loader::kBMn ? smem_desc_sw128(b0 + k * 2048, 8192, 1024)
-                                               : smem_desc_sw128(b0 + k * 32, 16, 1024);
-              umma_f16_pair(tmem_base + h * BN, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
-            }
-          }
-          if (!ok) break;
-          const uint32_t eb = smem_u32(&bars->empty[stage]);
-          umma_commit_pair(eb);
-          umma_commit_pair(mapa_shared(eb, 1));
+          issue_half(0, stage, kb);
+          issue_half(1, stage, kb);
+          release(stage);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
