@@ -1,7 +1,7 @@
 """Benchmark of the dense-contraction path on B200; prints ONE JSON line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl choreo|reference]
-                    [--workload auto|gemm8192|sharded]
+                    [--workload auto|gemm8192|sharded|custom|smallk|conv|relu]
 
 Workloads (inputs are seeded synthetic data of the configuration's shapes and
 distributions; nothing is read from disk):
@@ -11,18 +11,26 @@ distributions; nothing is read from disk):
             fused with ReLU, bf16 output; rows split across the N ranks
             (strong scaling: total work fixed), B and bias replicated, no
             collective on the data path. The default at N > 1.
-One step = one GEMM launch over the whole workload (per rank: its slab).
+  custom    GEMM of --shape MxNxK and --dtype (U[-1,1], NN).
+  smallk    fp16 GEMM 16384 x 16384 x 128: output-write (HBM) bound.
+  conv      implicit-GEMM conv2d NHWC fp16, N=32, 56x56, C=K=256, 3x3, s1 p1,
+            activations U[0,1], weights N(0, 1/48), bias N(0, 0.1) + ReLU.
+  relu      elementwise ReLU over 2^28 fp16 values (HBM bound).
+One step = one launch of the path over the whole workload (per rank: its slab).
 
-value : whole-job TFLOP/s with inputs resident in HBM; K steps timed with CUDA
-        events on the launching stream between barrier + synchronize, max over
-        ranks. A and B together exceed the 126 MB L2, so no flush is needed.
+value : whole-job throughput with inputs resident in HBM; K steps timed with
+        CUDA events on the launching stream between barrier + synchronize,
+        max over ranks. Where the inputs fit in the 126 MB L2 (conv, smallk),
+        a 256 MB buffer is written between steps and each launch is timed by
+        its own event pair; elsewhere the inputs exceed the L2.
 e2e   : the same metric through the C ABI with pinned HOST buffers: every step
-        copies A (slab) and B (+bias) host->device, runs the GEMM and copies C
+        copies the inputs host->device, runs the launch and copies the output
         back, all inside the timed region.
-cpu_baseline : the reference's own CPU operator* (include/choreo-ir/choreo-ir.hpp
-        :71-101, compiled from its sources into oracle/_ref) on a bounded row
-        sample, on the host's cores; the oracle's C restatement when the
-        reference library is absent.
+cpu_baseline : the reference's own CPU path (operator*, relu from
+        include/choreo-ir/choreo-ir.hpp, compiled from its sources into
+        oracle/_ref) on a bounded sample, on the host's cores; the oracle's C
+        restatement where the reference library is absent or has no such
+        entry (conv: the loop of benchmark/kernels/gemm_example.cu:208-253).
 --impl reference : that reference CPU path alone, as the comparison arm.
 """
 from __future__ import annotations
@@ -43,6 +51,8 @@ sys.path.insert(0, str(ROOT))
 
 F16, F32, BF16 = 8, 9, 11
 NOMINAL_DENSE_TFLOPS = 2250.0
+HEADLINE_METRIC = "fp16 GEMM TFLOP/s @8192^3 and % of B200 dense peak; sharded GEMM at 1/2/4/8 GPU"
+L2_BYTES = 126 * 1024 * 1024
 
 
 # ----------------------------------------------------------------- helpers
@@ -54,44 +64,91 @@ def load_choreo():
     return mod
 
 
+def _gemm(workload, m, n, k, dtype, dist, bias, relu):
+    return dict(kind="gemm", workload=workload, m_total=m, n=n, k=k, dtype=dtype, dist=dist, bias=bias,
+                relu=relu, layout="NN")
+
+
 def workload_spec(name: str, world: int, shape: str | None = None, dtype: str = "f16") -> dict:
     if name == "custom":
         m, n, k = (int(x) for x in (shape or "4096x4096x4096").lower().split("x"))
-        return dict(workload=f"gemm_{dtype}_{m}x{n}x{k}", m_total=m, n=n, k=k, dtype=dtype,
-                    dist="U[-1,1]", bias=False, relu=False, layout="NN")
+        return _gemm(f"gemm_{dtype}_{m}x{n}x{k}", m, n, k, dtype, "U[-1,1]", False, False)
     if name == "gemm8192":
-        return dict(workload="gemm_f16_8192x8192x8192", m_total=8192, n=8192, k=8192, dtype="f16",
-                    dist="U[-1,1]", bias=False, relu=False, layout="NN")
+        return _gemm("gemm_f16_8192x8192x8192", 8192, 8192, 8192, "f16", "U[-1,1]", False, False)
     if name == "sharded":
-        return dict(workload="rowsharded_gemm_bf16_65536x8192x8192_bias_relu", m_total=65536, n=8192, k=8192,
-                    dtype="bf16", dist="U[-0.5,0.5]", bias=True, relu=True, layout="NN")
+        return _gemm("rowsharded_gemm_bf16_65536x8192x8192_bias_relu", 65536, 8192, 8192, "bf16",
+                     "U[-0.5,0.5]", True, True)
+    if name == "smallk":
+        return _gemm("gemm_f16_16384x16384x128", 16384, 16384, 128, "f16", "U[-1,1]", False, False)
+    if name == "conv":
+        return dict(kind="conv", workload="conv2d_f16_n32_56x56_c256_k256_3x3_bias_relu", n=32, h=56, w=56,
+                    c=256, k=256, r=3, s=3, stride=1, pad=1, dtype="f16", bias=True, relu=True)
+    if name == "relu":
+        return dict(kind="relu", workload="relu_f16_268435456", numel=1 << 28, dtype="f16")
     raise SystemExit(f"unknown workload {name}")
+
+
+def spec_flops_bytes(spec: dict, rows: int | None = None) -> tuple[float, float]:
+    """Algorithmic FLOPs and HBM bytes of one launch (rows: this rank's slab)."""
+    if spec["kind"] == "gemm":
+        m = rows if rows is not None else spec["m_total"]
+        n, k = spec["n"], spec["k"]
+        return 2.0 * m * n * k, 2.0 * (m * k + k * n + m * n) + (2.0 * n if spec["bias"] else 0.0)
+    if spec["kind"] == "conv":
+        npix = spec["n"] * spec["h"] * spec["w"]          # stride 1, same padding
+        red = spec["r"] * spec["s"] * spec["c"]
+        return (2.0 * npix * spec["k"] * red,
+                2.0 * (npix * spec["c"] + spec["k"] * red + npix * spec["k"] + spec["k"]))
+    return 0.0, 4.0 * spec["numel"]
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    return json.loads(p.read_text()) if p.exists() else {}
 
 
 def measured_peak(timed_seconds: float) -> tuple[float, str]:
     """Dense bf16/fp16 tensor peak to report against: the pool's measured
     cuBLAS figure, burst for a short timed region, sustained for a long one."""
-    p = ROOT / "MEASURED_PEAKS.json"
-    if p.exists():
-        d = json.loads(p.read_text())
+    d = measured_peaks()
+    if d:
         if timed_seconds > 2.0 and d.get("bf16_tflops_sustained"):
             return float(d["bf16_tflops_sustained"]), "measured (sustained cuBLAS bf16)"
         return float(d["bf16_tflops"]), "measured (burst cuBLAS bf16)"
     return 1590.0, "fallback"
 
 
-def profiled_traffic(workload: str):
+def measured_hbm() -> tuple[float, str]:
+    d = measured_peaks()
+    if d.get("hbm_gbs"):
+        return float(d["hbm_gbs"]), "measured (copy, read+write bytes)"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(workload: str, units: float | None = None):
     """DRAM bytes per launch of the dominant kernel from the committed ncu
-    summary (a `dram_bytes_per_launch: <n>` line), else None."""
+    summary (a `dram_bytes_per_launch: <n>` line). A summary captured on a
+    smaller slab than the launch's says so with `captured_units: <rows>`, and
+    the figure is scaled by units / captured_units. None without a summary."""
     f = ROOT / "profiles" / f"{workload}.md"
-    if f.exists():
-        for line in f.read_text().splitlines():
-            if line.strip().startswith("dram_bytes_per_launch:"):
+    if not f.exists():
+        return None
+    vals = {}
+    for line in f.read_text().splitlines():
+        s = line.strip()
+        for key in ("dram_bytes_per_launch:", "captured_units:"):
+            if s.startswith(key):
                 try:
-                    return int(float(line.split(":", 1)[1].strip().split()[0]))
-                except ValueError:
-                    return None
-    return None
+                    vals[key] = float(s.split(":", 1)[1].strip().split()[0])
+                except (ValueError, IndexError):
+                    pass
+    t = vals.get("dram_bytes_per_launch:")
+    if t is None:
+        return None
+    cu = vals.get("captured_units:")
+    if cu and units:
+        t = t * units / cu
+    return int(t)
 
 
 class ClockSampler:
@@ -137,87 +194,283 @@ class ClockSampler:
             self.proc.kill()
         inside = [s for s in self.samples if any(a - 0.06 <= s[0] <= b + 0.06 for a, b in self.marks)]
         use = inside or self.samples
-        sm, mx, reasons = [], [], set()
+        sm, mx, pw, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for s in use:
             try:
                 sm.append(float(s[2]))
                 mx.append(float(s[3]))
+                pw.append(float(s[4]))
             except (ValueError, IndexError):
                 continue
             for nm, v in zip(names, s[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "power_w_median": statistics.median(pw) if pw else None,
                 "reasons": sorted(reasons), "samples": len(use), "samples_in_timed_region": len(inside)}
 
 
 # ----------------------------------------------------------------- reference CPU path
 def reference_cpu_sample(spec: dict, seconds_target: float, nthreads: int | None = None) -> dict:
-    """Times the reference CPU operator* on a bounded sample of the workload:
-    `rows` rows of A (one per thread) against a column slice of B, chosen so
-    one call takes about `seconds_target`. Per element the arithmetic is the
-    reference's (fp16/bf16 accumulation in k order)."""
+    """A bounded sample of the workload for the reference CPU path, sized so
+    one call takes about `seconds_target`:
+      gemm: `rows` rows of A (one per thread) against a column slice of B;
+            per element the arithmetic is the reference operator*'s (16-bit
+            accumulation in k order);
+      conv: a run of output pixels through the reference conv loop;
+      relu: a prefix of the tensor through the reference relu.
+    Returns the inputs plus `units` (FLOPs, or bytes for relu) per call."""
+    from oracle import oracle as orc
+    threads = nthreads or orc.threads()
+    if spec["kind"] == "gemm":
+        dt = F16 if spec["dtype"] == "f16" else BF16
+        lo, hi = (-1.0, 1.0) if spec["dist"] == "U[-1,1]" else (-0.5, 0.5)
+        k, n = spec["k"], spec["n"]
+        use_ref = orc.ref is not None
+        a1 = orc.to_bits(orc.uniform((1, k), lo, hi, 1), dt)
+        b1 = orc.to_bits(orc.uniform((k, 256), lo, hi, 2), dt)
+        t0 = time.perf_counter()
+        orc.ref_matmul(a1, b1, dt, nthreads=1, use_reference_lib=use_ref)
+        per_elem = (time.perf_counter() - t0) / 256
+        # one row per thread per pass; widen the column slice, then add rows,
+        # until a call is expected to take about seconds_target
+        elems = max(64.0, seconds_target / max(per_elem, 1e-9))
+        cols = int(min(n, elems))
+        rows = threads * max(1, int(elems // n))
+        a = orc.to_bits(orc.uniform((rows, k), lo, hi, 3), dt)
+        b = orc.to_bits(orc.uniform((k, cols), lo, hi, 4), dt)
+        return dict(kind="gemm", a=a, b=b, dt=dt, rows=rows, cols=cols, threads=threads, use_ref=use_ref,
+                    units=2.0 * rows * cols * k)
+    if spec["kind"] == "conv":
+        x = orc.to_bits(orc.uniform((1, spec["h"], spec["w"], spec["c"]), 0.0, 1.0, 5), F16)
+        w = orc.to_bits(orc.normal((spec["k"], spec["r"], spec["s"], spec["c"]), 0.0, 1.0 / 48, 6), F16)
+        t0 = time.perf_counter()
+        orc.ref_conv2d_f16(x, w, spec["stride"], spec["pad"], pix=(0, 1), nthreads=1)
+        per_pix = time.perf_counter() - t0
+        npix = int(min(spec["h"] * spec["w"], max(threads, threads * seconds_target / max(per_pix, 1e-9))))
+        red = spec["r"] * spec["s"] * spec["c"]
+        return dict(kind="conv", x=x, w=w, npix=npix, threads=threads, use_ref=False,
+                    units=2.0 * npix * spec["k"] * red, stride=spec["stride"], pad=spec["pad"])
+    # relu: the reference relu is a single-threaded loop
+    use_ref = orc.ref is not None
+    n1 = 1 << 22
+    x = orc.to_bits(orc.uniform((n1,), -1.0, 1.0, 7), F16)
+    t0 = time.perf_counter()
+    _relu_ref(x, use_ref)
+    per = (time.perf_counter() - t0) / n1
+    n = int(min(spec["numel"], max(n1, seconds_target / max(per, 1e-12))))
+    x = orc.to_bits(orc.uniform((n,), -1.0, 1.0, 8), F16)
+    return dict(kind="relu", x=x, n=n, threads=1, use_ref=use_ref, units=4.0 * n)
+
+
+def _relu_ref(x, use_ref: bool):
     import numpy as np
     from oracle import oracle as orc
-    dt = F16 if spec["dtype"] == "f16" else BF16
-    lo, hi = (-1.0, 1.0) if spec["dist"] == "U[-1,1]" else (-0.5, 0.5)
-    threads = nthreads or orc.threads()
-    k, n = spec["k"], spec["n"]
-    use_ref = orc.ref is not None
-    # calibrate: one row x 256 columns on one thread
-    a1 = orc.to_bits(orc.uniform((1, k), lo, hi, 1), dt)
-    b1 = orc.to_bits(orc.uniform((k, 256), lo, hi, 2), dt)
-    t0 = time.perf_counter()
-    orc.ref_matmul(a1, b1, dt, nthreads=1, use_reference_lib=use_ref)
-    per_elem = (time.perf_counter() - t0) / 256
-    # one row per thread per pass; widen the column slice, then add rows, until
-    # a call is expected to take about seconds_target
-    elems = max(64.0, seconds_target / max(per_elem, 1e-9))
-    cols = int(min(n, elems))
-    rows = threads * max(1, int(elems // n))
-    a = orc.to_bits(orc.uniform((rows, k), lo, hi, 3), dt)
-    b = orc.to_bits(orc.uniform((k, cols), lo, hi, 4), dt)
-    return dict(a=a, b=b, dt=dt, rows=rows, cols=cols, threads=threads, use_ref=use_ref,
-                flops=2.0 * rows * cols * k)
+    if use_ref:
+        out = np.empty_like(x)
+        rc = orc.ref.choreo_ref_relu_f16(x.ctypes.data, out.ctypes.data, x.size)
+        if rc != 0:
+            raise RuntimeError(f"reference relu failed ({rc})")
+        return out
+    return orc.ref_relu(x, F16)
 
 
 def run_reference_sample(s: dict) -> float:
     from oracle import oracle as orc
     t0 = time.perf_counter()
-    orc.ref_matmul(s["a"], s["b"], s["dt"], nthreads=s["threads"], use_reference_lib=s["use_ref"])
+    if s["kind"] == "gemm":
+        orc.ref_matmul(s["a"], s["b"], s["dt"], nthreads=s["threads"], use_reference_lib=s["use_ref"])
+    elif s["kind"] == "conv":
+        orc.ref_conv2d_f16(s["x"], s["w"], s["stride"], s["pad"], pix=(0, s["npix"]), nthreads=s["threads"])
+    else:
+        _relu_ref(s["x"], s["use_ref"])
     return time.perf_counter() - t0
 
 
 def sample_text(s: dict, spec: dict) -> str:
-    src = ("reference operator* compiled from its sources (oracle/_ref)" if s["use_ref"]
-           else "oracle C restatement of the reference operator*")
-    return (f"{s['rows']} rows x {s['cols']} of {spec['n']} columns of C at K={spec['k']} "
-            f"({spec['dtype']}, accumulation in {spec['dtype']} as the reference does); {src}; "
-            f"{s['threads']} host threads splitting the rows")
+    if s["kind"] == "gemm":
+        src = ("reference operator* compiled from its sources (oracle/_ref)" if s["use_ref"]
+               else "oracle C restatement of the reference operator*")
+        return (f"{s['rows']} rows x {s['cols']} of {spec['n']} columns of C at K={spec['k']} "
+                f"({spec['dtype']}, accumulation in {spec['dtype']} as the reference does); {src}; "
+                f"{s['threads']} host threads splitting the rows")
+    if s["kind"] == "conv":
+        return (f"{s['npix']} output pixels x {spec['k']} channels of image 0 (3x3x{spec['c']} reduction, fp16 "
+                f"accumulation as the reference conv loop does); oracle C restatement of the reference's "
+                f"conv2d_kernel loop (the reference has no host conv entry to compile); "
+                f"{s['threads']} host threads splitting the pixels")
+    src = "reference relu compiled from its sources (oracle/_ref)" if s["use_ref"] else "oracle C restatement"
+    return f"{s['n']} fp16 values; {src}; single-threaded as the reference loop is"
 
 
 # ----------------------------------------------------------------- main arms
+def metric_of(spec: dict) -> tuple[str, str]:
+    if spec["kind"] == "relu":
+        return "elementwise ReLU GB/s (fp16, 2^28 values)", "GB/s"
+    if spec["kind"] == "conv":
+        return "implicit-GEMM conv2d TFLOP/s (NHWC fp16 32x56x56x256, 3x3, bias+ReLU)", "TFLOP/s"
+    if spec["workload"] in ("gemm_f16_8192x8192x8192", "rowsharded_gemm_bf16_65536x8192x8192_bias_relu"):
+        return HEADLINE_METRIC, "TFLOP/s"
+    return f"GEMM TFLOP/s ({spec['workload']})", "TFLOP/s"
+
+
 def bench_reference(args, spec: dict, world: int, rank: int) -> None:
     if rank != 0:
         return
+    metric, unit = metric_of(spec)
     s = reference_cpu_sample(spec, seconds_target=float(os.environ.get("CHOREO_REF_STEP_SECONDS", "1.0")))
     for _ in range(args.warmup):
         run_reference_sample(s)
     times = [run_reference_sample(s) for _ in range(args.steps)]
     total = sum(times)
-    value = s["flops"] * args.steps / total / 1e12
+    scale = 1e9 if unit == "GB/s" else 1e12
+    value = s["units"] * args.steps / total / scale
     line = {
-        "metric": args.metric, "value": value, "unit": "TFLOP/s", "impl": "reference", "n_gpus": world,
+        "metric": metric, "value": value, "unit": unit, "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
-        "higher_is_better": True, "scaling": "strong" if spec["m_total"] == 65536 else "weak",
+        "higher_is_better": True, "scaling": "strong" if spec.get("m_total") == 65536 else "weak",
         "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
-        "config": {**{k: v for k, v in spec.items()}, "timed": "CPU wall clock per step over a bounded sample"},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": s["threads"],
+        "config": {**spec, "timed": "CPU wall clock per step over a bounded sample"},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": s["threads"],
                          "kind": "reference" if s["use_ref"] else "port", "sample": sample_text(s, spec)},
-        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+class Case:
+    """Device buffers and the step functions of one workload on one rank."""
+    step = None        # one launch on device-resident inputs
+    e2e_step = None    # host->device inputs, the launch, device->host output
+    h2d = d2h = 0
+    rows = None        # this rank's slab (GEMM rows)
+    units_total = 0.0  # whole-job FLOPs (or bytes) per step
+    flops = bytes_ = 0.0  # this rank's algorithmic FLOPs / bytes per launch
+    flush = False      # inputs + outputs fit in L2: flush between timed launches
+    info: dict = {}
+
+
+def _pinned_copy(t):
+    import torch
+    h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    h.copy_(t)
+    return h
+
+
+def setup_gemm(cb, spec, world, rank, dev, stream) -> Case:
+    import torch
+    dt = torch.float16 if spec["dtype"] == "f16" else torch.bfloat16
+    lo, hi = (-1.0, 1.0) if spec["dist"] == "U[-1,1]" else (-0.5, 0.5)
+    M_total, N, K = spec["m_total"], spec["n"], spec["k"]
+    r0, rows = cb.shard_rows(M_total, world, rank)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    a = torch.empty(rows, K, device=dev).uniform_(lo, hi, generator=g).to(dt)
+    g.manual_seed(99)  # B and bias are replicas: same seed on every rank
+    b = torch.empty(K, N, device=dev).uniform_(lo, hi, generator=g).to(dt)
+    bias = torch.empty(N, device=dev).normal_(0.0, 0.1, generator=g).to(dt) if spec["bias"] else None
+    c = torch.empty(rows, N, device=dev, dtype=dt)
+    desc = cb.make_gemm_desc(a, b, c, m=rows, n=N, k=K, bias=bias, relu=spec["relu"])
+    q = cb.gemm_query(desc)
+    assert q.workspace_bytes == 0
+    case = Case()
+    case.step = lambda: cb.gemm_desc(desc, stream=stream)
+    a_h, b_h = _pinned_copy(a), _pinned_copy(b)
+    bias_h = _pinned_copy(bias) if bias is not None else None
+    c_h = torch.empty(rows, N, dtype=dt, pin_memory=True)
+
+    def e2e():
+        a.copy_(a_h, non_blocking=True)
+        b.copy_(b_h, non_blocking=True)
+        if bias is not None:
+            bias.copy_(bias_h, non_blocking=True)
+        cb.gemm_desc(desc, stream=stream)
+        c_h.copy_(c, non_blocking=True)
+
+    case.e2e_step = e2e
+    case.h2d = sum(t.numel() * t.element_size() for t in (a_h, b_h, bias_h) if t is not None)
+    case.d2h = c_h.numel() * c_h.element_size()
+    case.rows = rows
+    case.flops, case.bytes_ = spec_flops_bytes(spec, rows)
+    case.units_total = spec_flops_bytes(spec)[0]
+    case.flush = case.bytes_ - 2.0 * rows * N <= L2_BYTES      # A + B (+ bias) fit in L2
+    case.info = {
+        "m": M_total, "n": N, "k": K, "layout": spec["layout"],
+        "inputs": f"{spec['dist']} seeded on device; fp32 accumulation; {spec['dtype']} output",
+        "epilogue": "bias+ReLU" if spec["bias"] else "none",
+        "parallelism": f"row-sharded over {world} GPU(s), B replicated, no collective" if world > 1 else "single GPU",
+        "rows_per_rank": rows, "tile": f"{q.tile_m}x{q.tile_n}x{q.tile_k}", "cluster": q.cluster_m,
+        "stages": q.stages, "grid": q.grid_x,
+    }
+    return case
+
+
+def setup_conv(cb, spec, world, rank, dev, stream) -> Case:
+    import torch
+    g = torch.Generator(device=dev)
+    g.manual_seed(5 + rank)
+    x = torch.empty(spec["n"], spec["h"], spec["w"], spec["c"], device=dev).uniform_(0, 1, generator=g).half()
+    g.manual_seed(6)
+    wt = torch.empty(spec["k"], spec["r"], spec["s"], spec["c"], device=dev).normal_(
+        0, 1 / 48.0, generator=g).half()
+    bias = torch.empty(spec["k"], device=dev).normal_(0, 0.1, generator=g).half()
+    out = torch.empty(spec["n"], spec["h"], spec["w"], spec["k"], device=dev, dtype=torch.float16)
+    d = cb.conv_desc(x, wt, out, stride=spec["stride"], padding=spec["pad"], bias=bias, relu=spec["relu"])
+    q = cb.conv2d_query(d)
+    assert q.workspace_bytes == 0
+    case = Case()
+    case.step = lambda: cb.conv2d_desc(d, stream=stream)
+    x_h, w_h, b_h = _pinned_copy(x), _pinned_copy(wt), _pinned_copy(bias)
+    o_h = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+
+    def e2e():
+        x.copy_(x_h, non_blocking=True)
+        wt.copy_(w_h, non_blocking=True)
+        bias.copy_(b_h, non_blocking=True)
+        case.step()
+        o_h.copy_(out, non_blocking=True)
+
+    case.e2e_step = e2e
+    case.h2d = sum(t.numel() * t.element_size() for t in (x_h, w_h, b_h))
+    case.d2h = o_h.numel() * o_h.element_size()
+    case.flops, case.bytes_ = spec_flops_bytes(spec)
+    case.units_total = case.flops * world
+    case.flush = case.bytes_ - 2.0 * out.numel() <= L2_BYTES    # activations + weights fit in L2
+    case.info = {"n": spec["n"], "h": spec["h"], "w": spec["w"], "c": spec["c"], "k": spec["k"],
+                 "rs": f"{spec['r']}x{spec['s']}", "stride": spec["stride"], "pad": spec["pad"],
+                 "inputs": "activations U[0,1], weights N(0,1/48), bias N(0,0.1), seeded on device; "
+                           "fp32 accumulation; fp16 output",
+                 "epilogue": "bias+ReLU", "parallelism": "single GPU" if world == 1 else
+                 f"{world} independent replicas (no collective)",
+                 "tile": f"{q.tile_m}x{q.tile_n}x{q.tile_k}", "cluster": q.cluster_m, "stages": q.stages,
+                 "grid": q.grid_x}
+    return case
+
+
+def setup_relu(cb, spec, world, rank, dev, stream) -> Case:
+    import torch
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    x = torch.empty(spec["numel"], device=dev).uniform_(-1, 1, generator=g).half()
+    y = torch.empty_like(x)
+    case = Case()
+    case.step = lambda: cb.relu(x, y, stream=stream)
+    x_h = _pinned_copy(x)
+    y_h = torch.empty_like(x_h, pin_memory=True)
+
+    def e2e():
+        x.copy_(x_h, non_blocking=True)
+        cb.relu(x, y, stream=stream)
+        y_h.copy_(y, non_blocking=True)
+
+    case.e2e_step = e2e
+    case.h2d = case.d2h = x_h.numel() * 2
+    case.flops, case.bytes_ = spec_flops_bytes(spec)
+    case.units_total = case.bytes_ * world
+    case.info = {"numel": spec["numel"], "inputs": "U[-1,1] seeded on device",
+                 "parallelism": "single GPU" if world == 1 else f"{world} independent replicas"}
+    return case
 
 
 def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> None:
@@ -227,86 +480,72 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
     cb = load_choreo()
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    dt = torch.float16 if spec["dtype"] == "f16" else torch.bfloat16
-    lo, hi = (-1.0, 1.0) if spec["dist"] == "U[-1,1]" else (-0.5, 0.5)
-    M_total, N, K = spec["m_total"], spec["n"], spec["k"]
-    r0, rows = cb.shard_rows(M_total, world, rank)
-
-    g = torch.Generator(device=dev)
-    g.manual_seed(1234 + rank)
-    a = torch.empty(rows, K, device=dev).uniform_(lo, hi, generator=g).to(dt)
-    g.manual_seed(99)  # B and bias are replicas: same seed on every rank
-    b = torch.empty(K, N, device=dev).uniform_(lo, hi, generator=g).to(dt)
-    bias = torch.empty(N, device=dev).normal_(0.0, 0.1, generator=g).to(dt) if spec["bias"] else None
-    c = torch.empty(rows, N, device=dev, dtype=dt)
     stream = torch.cuda.current_stream(dev)
-    desc = cb.make_gemm_desc(a, b, c, m=rows, n=N, k=K, bias=bias, relu=spec["relu"])
-    q = cb.gemm_query(desc)
-    assert q.workspace_bytes == 0
+    setup = {"gemm": setup_gemm, "conv": setup_conv, "relu": setup_relu}[spec["kind"]]
+    case = setup(cb, spec, world, rank, dev, stream)
+    metric, unit = metric_of(spec)
+    hbm_bound = spec["kind"] == "relu"
+    if spec["kind"] == "gemm":
+        peak_tf = measured_peak(0.0)[0]
+        hbm_gbs = measured_hbm()[0]
+        hbm_bound = case.flops / case.bytes_ < peak_tf * 1e12 / (hbm_gbs * 1e9)
+    flush_buf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if case.flush else None
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    def step():
-        cb.gemm_desc(desc, stream=stream)
+    def timed(fn, steps: int) -> float:
+        """Device milliseconds of `steps` calls of fn on `stream`. With a
+        flush, each call is bracketed by its own events and the L2 is
+        overwritten between calls, outside the events."""
+        if flush_buf is None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(steps):
+                fn()
+            e1.record(stream)
+            e1.synchronize()
+            return e0.elapsed_time(e1)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for s, e in evs:
+            flush_buf.fill_(1.0)
+            s.record(stream)
+            fn()
+            e.record(stream)
+        evs[-1][1].synchronize()
+        return sum(s.elapsed_time(e) for s, e in evs)
 
     # ---------------------------------------------------------- device-resident timing
     for _ in range(args.warmup):
-        step()
+        case.step()
     cb.sync_status(stream)
     visible = os.environ.get("CUDA_VISIBLE_DEVICES")
     phys = [int(x) for x in visible.split(",")] if visible else list(range(max(world, 1)))
-    sampler = ClockSampler(phys[:world] if rank == 0 else [phys[local_rank]]) if rank == 0 else None
+    sampler = ClockSampler(phys[:world]) if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
     barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_wall0 = time.time()
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
+    ms = timed(case.step, args.steps)
     barrier()
     t_wall1 = time.time()
     cb.sync_status(stream)
-    ms = e0.elapsed_time(e1)
     if sampler:
         sampler.mark(t_wall0, t_wall1)
 
     # ---------------------------------------------------------- end to end from pinned host buffers
-    a_h = torch.empty(rows, K, dtype=dt, pin_memory=True)
-    a_h.copy_(a)
-    b_h = torch.empty(K, N, dtype=dt, pin_memory=True)
-    b_h.copy_(b)
-    bias_h = None
-    if bias is not None:
-        bias_h = torch.empty(N, dtype=dt, pin_memory=True)
-        bias_h.copy_(bias)
-    c_h = torch.empty(rows, N, dtype=dt, pin_memory=True)
-    h2d = a_h.numel() * a_h.element_size() + b_h.numel() * b_h.element_size() + \
-        (bias_h.numel() * bias_h.element_size() if bias_h is not None else 0)
-    d2h = c_h.numel() * c_h.element_size()
-
-    def e2e_step():
-        a.copy_(a_h, non_blocking=True)
-        b.copy_(b_h, non_blocking=True)
-        if bias is not None:
-            bias.copy_(bias_h, non_blocking=True)
-        cb.gemm_desc(desc, stream=stream)
-        c_h.copy_(c, non_blocking=True)
-
     e2e_steps = max(1, min(args.steps, 20))
     for _ in range(max(1, min(args.warmup, 3))):
-        e2e_step()
+        case.e2e_step()
     barrier()
     t_wall2 = time.time()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
     for _ in range(e2e_steps):
-        e2e_step()
+        case.e2e_step()
     e3.record(stream)
     barrier()
     t_wall3 = time.time()
@@ -322,13 +561,23 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max, ms_e2e_max = float(t[0]), float(t[1])
-    flops_total = 2.0 * M_total * N * K
-    value = flops_total * args.steps / (ms_max * 1e-3) / 1e12
-    e2e_value = flops_total * e2e_steps / (ms_e2e_max * 1e-3) / 1e12
-    # dominant kernel on this rank: one launch per step, back to back on `stream`
+    scale = 1e9 if unit == "GB/s" else 1e12
+    value = case.units_total * args.steps / (ms_max * 1e-3) / scale
+    e2e_value = case.units_total * e2e_steps / (ms_e2e_max * 1e-3) / scale
+    # dominant kernel on this rank: one launch per step on `stream`
     per_launch_ms = ms / args.steps
-    achieved = 2.0 * rows * N * K / (per_launch_ms * 1e-3) / 1e12
-    peak, peak_src = measured_peak(ms * 1e-3)
+    if hbm_bound:
+        peak, peak_src = measured_hbm()
+        roof = {"bound": "hbm", "achieved": case.bytes_ / (per_launch_ms * 1e-3) / 1e9, "peak": peak,
+                "unit": "GB/s", "algorithmic_bytes_per_launch": case.bytes_}
+    else:
+        peak, peak_src = measured_peak(ms * 1e-3)
+        roof = {"bound": "tensor", "achieved": case.flops / (per_launch_ms * 1e-3) / 1e12, "peak": peak,
+                "unit": "TFLOP/s", "algorithmic_flops_per_launch": case.flops}
+    roof["frac"] = roof["achieved"] / peak
+    roof["peak_source"] = peak_src
+    roof["traffic"] = profiled_traffic(spec["workload"], case.rows)
+    roof["per_launch_ms"] = per_launch_ms
 
     if rank != 0:
         return
@@ -336,43 +585,35 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
     if world == 1 and not args.no_cpu_baseline:
         s = reference_cpu_sample(spec, seconds_target=float(os.environ.get("CHOREO_CPU_BASELINE_SECONDS", "12")))
         secs = run_reference_sample(s)
-        cpu = {"value": s["flops"] / secs / 1e12, "unit": "TFLOP/s", "cores": s["threads"],
+        cpu = {"value": s["units"] / secs / scale, "unit": unit, "cores": s["threads"],
                "kind": "reference" if s["use_ref"] else "port", "sample": sample_text(s, spec),
                "seconds": round(secs, 2)}
+    config = {"workload": spec["workload"], **case.info,
+              "l2": ("L2 flushed (256 MB written) between timed launches; per-launch events" if case.flush
+                     else "inputs larger than the 126 MB L2 (no flush needed)")}
     line = {
-        "metric": args.metric,
+        "metric": metric,
         "value": value,
-        "unit": "TFLOP/s",
+        "unit": unit,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": ms_max / args.steps,
         "higher_is_better": True,
-        "scaling": "strong" if spec["m_total"] == 65536 and world > 1 else "weak",
+        "scaling": "strong" if spec.get("m_total") == 65536 and world > 1 else "weak",
         "vs_baseline": None,
         "dtype": spec["dtype"],
         "data": "synthetic",
-        "pct_of_nominal_dense_peak": 100.0 * value / (NOMINAL_DENSE_TFLOPS * world),
-        "config": {
-            "workload": spec["workload"], "m": M_total, "n": N, "k": K, "layout": spec["layout"],
-            "inputs": f"{spec['dist']} seeded on device; fp32 accumulation; {spec['dtype']} output",
-            "epilogue": "bias+ReLU" if spec["bias"] else "none",
-            "parallelism": f"row-sharded over {world} GPU(s), B replicated, no collective" if world > 1 else "single GPU",
-            "rows_per_rank": rows, "tile": f"{q.tile_m}x{q.tile_n}x{q.tile_k}", "stages": q.stages,
-            "grid": q.grid_x, "l2": "inputs larger than the 126 MB L2 (no flush needed)",
-        },
-        "roofline": {
-            "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-            "peak_source": peak_src, "traffic": profiled_traffic(spec["workload"]),
-            "algorithmic_flops_per_launch": 2.0 * rows * N * K,
-            "per_launch_ms": per_launch_ms,
-        },
-        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+        "config": config,
+        "roofline": roof,
+        "e2e": {"value": e2e_value, "unit": unit, "h2d_bytes_per_step": case.h2d, "d2h_bytes_per_step": case.d2h,
                 "steps": e2e_steps, "ms_per_step": ms_e2e_max / e2e_steps},
         "gpu_launches": args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
+    if unit == "TFLOP/s":
+        line["pct_of_nominal_dense_peak"] = 100.0 * value / (NOMINAL_DENSE_TFLOPS * world)
     print(json.dumps(line), flush=True)
 
 
@@ -382,15 +623,15 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="choreo", choices=["choreo", "reference"])
-    ap.add_argument("--workload", default="auto", choices=["auto", "gemm8192", "sharded", "custom"])
+    ap.add_argument("--workload", default="auto",
+                    choices=["auto", "gemm8192", "sharded", "custom", "smallk", "conv", "relu"])
     ap.add_argument("--shape", default=None, help="MxNxK for --workload custom")
     ap.add_argument("--dtype", default="f16", choices=["f16", "bf16"], help="input/output type for --workload custom")
     ap.add_argument("--tile", default=None,
-                    help="force a kernel configuration: pair256, pair128, single256, single128 or single64")
+                    help="force a kernel configuration: wide256, pair256, pair128, single256, single128 or single64")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    args.metric = "fp16 GEMM TFLOP/s @8192^3 and % of B200 dense peak; sharded GEMM at 1/2/4/8 GPU"
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

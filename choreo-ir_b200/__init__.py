@@ -230,9 +230,13 @@ def conv2d_query(d: ConvDesc) -> LaunchConfig:
     return out
 
 
+def conv2d_desc(d: ConvDesc, workspace=None, workspace_bytes=0, stream=None) -> None:
+    check(lib.choreo_conv2d(C.byref(d), _ptr(workspace), workspace_bytes, _stream_ptr(stream)))
+
+
 def conv2d(x, w, out, *, stride=1, padding=1, dilation=1, bias=None, relu=False, alpha=1.0, stream=None) -> None:
     d = conv_desc(x, w, out, stride=stride, padding=padding, dilation=dilation, bias=bias, relu=relu, alpha=alpha)
-    check(lib.choreo_conv2d(C.byref(d), None, 0, _stream_ptr(stream)))
+    conv2d_desc(d, stream=stream)
 
 
 def relu(x, out, stream=None) -> None:

@@ -117,22 +117,64 @@ __device__ __forceinline__ void tile_coords(int64_t t, const TcParams& p, int& b
   nb = in / gm;
 }
 
+__device__ __forceinline__ void unpack2(uint32_t u, float& a, float& b, __half*) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u));
+  a = f.x;
+  b = f.y;
+}
+__device__ __forceinline__ void unpack2(uint32_t u, float& a, float& b, __nv_bfloat16*) {
+  const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+  a = f.x;
+  b = f.y;
+}
+
 // alpha * acc + beta * C + bias, then ReLU, for one 32-column chunk of one row.
+// Called by all 32 lanes of a warp together (lane = row within the warp's
+// slab): the chunk's bias is read once, lane j fetching column n_base + j, and
+// broadcast with shuffles.
 template <typename OutT>
 __device__ __forceinline__ void epilogue_values(const uint32_t (&r)[32], float (&v)[32], const OutT* crow,
-                                                int n_base, const TcParams& p, bool row_ok) {
+                                                int n_base, const TcParams& p, bool row_ok, int lane) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
   const bool full = (n_base + 32 <= p.n);
   if (p.beta != 0.f && row_ok) {
+    if (full && p.c_vec_ok) {
+      if constexpr (sizeof(OutT) == 2) {
+        const uint4* src = reinterpret_cast<const uint4*>(crow + n_base);
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (full || n_base + i < p.n) v[i] += p.beta * to_f32<OutT>(crow[n_base + i]);
+        for (int j = 0; j < 4; ++j) {
+          const uint4 q = src[j];
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float a, b;
+            unpack2(w[e], a, b, static_cast<OutT*>(nullptr));
+            v[8 * j + 2 * e] += p.beta * a;
+            v[8 * j + 2 * e + 1] += p.beta * b;
+          }
+        }
+      } else {
+        const float4* src = reinterpret_cast<const float4*>(crow + n_base);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 q = src[j];
+          v[4 * j + 0] += p.beta * q.x;
+          v[4 * j + 1] += p.beta * q.y;
+          v[4 * j + 2] += p.beta * q.z;
+          v[4 * j + 3] += p.beta * q.w;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (full || n_base + i < p.n) v[i] += p.beta * to_f32<OutT>(crow[n_base + i]);
+    }
   }
   if (p.bias != nullptr) {
+    const float bl = (n_base + lane < p.n) ? load_bias(p.bias, p.dtype_bias, n_base + lane) : 0.f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (full || n_base + i < p.n) v[i] += load_bias(p.bias, p.dtype_bias, n_base + i);
+    for (int i = 0; i < 32; ++i) v[i] += __shfl_sync(0xffffffffu, bl, i);
   }
   if (p.relu) {
 #pragma unroll
@@ -171,9 +213,9 @@ __device__ __forceinline__ void stage_row_32(const float (&v)[32], uint32_t row_
 // global stores: 16-byte vectors where legal, scalars at ragged edges).
 template <typename OutT>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], OutT* crow, int n_base,
-                                               const TcParams& p, bool row_ok) {
+                                               const TcParams& p, bool row_ok, int lane) {
   float v[32];
-  epilogue_values<OutT>(r, v, crow, n_base, p, row_ok);
+  epilogue_values<OutT>(r, v, crow, n_base, p, row_ok, lane);
   const bool full = (n_base + 32 <= p.n);
   if (!row_ok) return;
   if constexpr (sizeof(OutT) == 2) {
@@ -202,6 +244,31 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], OutT* cr
 #pragma unroll
   for (int i = 0; i < 32; ++i)
     if (n_base + i < p.n) crow[n_base + i] = from_f32<OutT>(v[i]);
+}
+
+// Number of 32-column TMEM chunks read per tcgen05.wait::ld in the epilogues:
+// several loads in flight hide the TMEM read latency.
+constexpr int kLdBatch = 4;
+
+// Epilogue of one warp's 32-row slab of a BN-column accumulator at TMEM
+// address `taddr`, with direct 16-byte stores (columns n0 .. n0 + BN).
+template <int BN, typename OutT>
+__device__ __forceinline__ void epilogue_slab_direct(uint32_t taddr, OutT* crow, int n0, const TcParams& p,
+                                                     bool row_ok, int lane) {
+  constexpr int kB = (BN / 32) < kLdBatch ? (BN / 32) : kLdBatch;
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN / 32; c0 += kB) {
+    if (n0 + c0 * 32 >= p.n) break;  // warp-uniform
+    uint32_t r[kB][32];
+#pragma unroll
+    for (int j = 0; j < kB; ++j) tmem_ld_32x32b_x32(taddr + (c0 + j) * 32, r[j]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      const int n_base = n0 + (c0 + j) * 32;
+      if (n_base < p.n) epilogue_chunk<OutT>(r[j], crow, n_base, p, row_ok, lane);
+    }
+  }
 }
 
 // Shared-memory bookkeeping beyond the stage ring.
@@ -368,15 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       OutT* crow = static_cast<OutT*>(p.c) + static_cast<int64_t>(b) * p.stride_c +
                    static_cast<int64_t>(row_ok ? row : 0) * p.ldc;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int n_base = nb * BN + c * 32;
-        if (n_base >= p.n) break;  // warp-uniform
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, r);
-        tmem_wait_ld();
-        epilogue_chunk<OutT>(r, crow, n_base, p, row_ok);
-      }
+      epilogue_slab_direct<BN, OutT>(taddr, crow, nb * BN, p, row_ok, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars->tmem_empty[buf]));
@@ -565,15 +624,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       OutT* crow = static_cast<OutT*>(p.c) + static_cast<int64_t>(b) * p.stride_c +
                    static_cast<int64_t>(row_ok ? row : 0) * p.ldc;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int n_base = nb * BN + c * 32;
-        if (n_base >= p.n) break;  // warp-uniform
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, r);
-        tmem_wait_ld();
-        epilogue_chunk<OutT>(r, crow, n_base, p, row_ok);
-      }
+      epilogue_slab_direct<BN, OutT>(taddr, crow, nb * BN, p, row_ok, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -602,8 +653,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // columns: a quarter less L2 -> SM operand traffic per FLOP than 256 x 256
 // tiles. With no room for a second accumulator, overlap comes from draining
 // the accumulator in halves: the epilogue releases half 0 as soon as it has
-// read it, and the next tile's first k-block issues its half-0 MMAs while the
-// epilogue is still reading half 1.
+// read it, and the next tile's first pipeline-depth k-blocks issue their
+// half-0 MMAs while the epilogue is still reading half 1.
 template <int STAGES>
 struct alignas(8) TcWideBarriers {
   uint64_t full[STAGES];
@@ -824,42 +875,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (p.c_tma) {
           // TMEM -> registers -> swizzled staging tile -> bulk tensor store (clipped at the edges).
           if (row0 < p.m) {  // warp-uniform
+            constexpr int kCpg = E / 32;  // 32-column chunks per staging row
 #pragma unroll 1
-            for (int g = 0; g < BN / E; ++g) {
-              const int n_base = nb * BN + g * E;
-              if (n_base >= p.n) break;  // warp-uniform
-              const uint32_t buf = stage_base + (store_iter & 1u) * 4096u;
-              if (lane == 0) bulk_wait_read_le1();  // the store issued two groups ago has read this buffer
-              __syncwarp();
+            for (int c0 = 0; c0 < BN / 32; c0 += kLdBatch) {
+              if (nb * BN + c0 * 32 >= p.n) break;  // warp-uniform
+              uint32_t r[kLdBatch][32];
 #pragma unroll
-              for (int c = 0; c < E / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(taddr + g * E + c * 32, r);
-                tmem_wait_ld();
-                float v[32];
-                epilogue_values<OutT>(r, v, crow, n_base + c * 32, p, row_ok);
-                stage_row_32<OutT>(v, buf + static_cast<uint32_t>(lane) * 128u, lane,
-                                   c * (32 * static_cast<int>(sizeof(OutT)) / 16));
+              for (int j = 0; j < kLdBatch; ++j) tmem_ld_32x32b_x32(taddr + (c0 + j) * 32, r[j]);
+              tmem_wait_ld();
+#pragma unroll
+              for (int gi = 0; gi < kLdBatch / kCpg; ++gi) {
+                const int n_base = nb * BN + c0 * 32 + gi * E;
+                if (n_base >= p.n) break;  // warp-uniform
+                const uint32_t buf = stage_base + (store_iter & 1u) * 4096u;
+                if (lane == 0) bulk_wait_read_le1();  // the store issued two groups ago has read this buffer
+                __syncwarp();
+#pragma unroll
+                for (int c = 0; c < kCpg; ++c) {
+                  float v[32];
+                  epilogue_values<OutT>(r[gi * kCpg + c], v, crow, n_base + c * 32, p, row_ok, lane);
+                  stage_row_32<OutT>(v, buf + static_cast<uint32_t>(lane) * 128u, lane,
+                                     c * (32 * static_cast<int>(sizeof(OutT)) / 16));
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                  tma_store_3d(&tma_c, buf, n_base, row0, b);
+                  bulk_commit_group();
+                }
+                ++store_iter;
               }
-              fence_proxy_async_smem();
-              __syncwarp();
-              if (lane == 0) {
-                tma_store_3d(&tma_c, buf, n_base, row0, b);
-                bulk_commit_group();
-              }
-              ++store_iter;
             }
           }
         } else {
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            const int n_base = nb * BN + c * 32;
-            if (n_base >= p.n) break;  // warp-uniform
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(taddr + c * 32, r);
-            tmem_wait_ld();
-            epilogue_chunk<OutT>(r, crow, n_base, p, row_ok);
-          }
+          epilogue_slab_direct<BN, OutT>(taddr, crow, nb * BN, p, row_ok, lane);
         }
         tc_fence_before();
         __syncwarp();
