@@ -99,7 +99,7 @@ ConvGeom geom(const choreo_conv_desc& d) {
 }
 
 constexpr int conv_stages(int bn) { return bn == 256 ? 4 : (bn == 128 ? 6 : 8); }
-constexpr int conv_pair_stages(int bn) { return bn == 256 ? 7 : 8; }
+constexpr int conv_pair_stages(int bn) { return bn == 256 ? 6 : 8; }
 constexpr int kConvWideStages = 4;
 
 template <typename OutT>
@@ -116,28 +116,28 @@ int launch_conv_wide(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
 }
 
 template <int BN, typename OutT>
-int launch_conv_one(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp, int grid,
-                    cudaStream_t stream) {
+int launch_conv_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& kp,
+                    int grid, cudaStream_t stream) {
   constexpr int STAGES = conv_stages(BN);
   constexpr int smem = tc_smem_bytes<BN, STAGES>();
   auto kern = tc_gemm_kernel<BN, STAGES, ConvLoader<BN, false>, OutT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(conv)");
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, kp);
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 conv launch");
   return CHOREO_OK;
 }
 
 template <int BN, typename OutT>
-int launch_conv_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp, int grid,
-                     cudaStream_t stream) {
+int launch_conv_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& kp,
+                     int grid, cudaStream_t stream) {
   constexpr int STAGES = conv_pair_stages(BN);
   constexpr int smem = tc_pair_smem_bytes<BN, STAGES>();
   auto kern = tc_gemm_pair_kernel<BN, STAGES, ConvLoader<BN / 2, true>, OutT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(conv pair)");
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, kp);
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 CTA-pair conv launch");
   return CHOREO_OK;
@@ -148,13 +148,13 @@ int conv_dispatch(const TcConfig& cfg, const CUtensorMap& ta, const CUtensorMap&
                   const TcParams& kp, int grid, cudaStream_t s) {
   if (cfg.wide) return launch_conv_wide<OutT>(ta, tb, tc, kp, grid, s);
   if (cfg.pair) {
-    if (cfg.bn == 256) return launch_conv_pair<256, OutT>(ta, tb, kp, grid, s);
-    return launch_conv_pair<128, OutT>(ta, tb, kp, grid, s);
+    if (cfg.bn == 256) return launch_conv_pair<256, OutT>(ta, tb, tc, kp, grid, s);
+    return launch_conv_pair<128, OutT>(ta, tb, tc, kp, grid, s);
   }
   switch (cfg.bn) {
-    case 256: return launch_conv_one<256, OutT>(ta, tb, kp, grid, s);
-    case 128: return launch_conv_one<128, OutT>(ta, tb, kp, grid, s);
-    default: return launch_conv_one<64, OutT>(ta, tb, kp, grid, s);
+    case 256: return launch_conv_one<256, OutT>(ta, tb, tc, kp, grid, s);
+    case 128: return launch_conv_one<128, OutT>(ta, tb, tc, kp, grid, s);
+    default: return launch_conv_one<64, OutT>(ta, tb, tc, kp, grid, s);
   }
 }
 
@@ -244,7 +244,7 @@ int launch_conv_tc(const choreo_conv_desc& d, cudaStream_t stream) {
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
   kp.c_tma = 0;
-  if (cfg.wide && kp.c_vec_ok) {
+  if (kp.c_vec_ok) {
     const uint64_t elem = static_cast<uint64_t>(ob);
     const uint64_t dims[3] = {static_cast<uint64_t>(d.k), static_cast<uint64_t>(g.m), 1};
     const uint64_t strides[2] = {static_cast<uint64_t>(d.k) * elem, static_cast<uint64_t>(g.m) * d.k * elem};

@@ -76,32 +76,32 @@ using namespace choreo_sm100;
 namespace {
 
 constexpr int stages_for(int bn) { return bn == 256 ? 4 : (bn == 128 ? 6 : 8); }
-constexpr int pair_stages_for(int bn) { return bn == 256 ? 7 : 8; }
+constexpr int pair_stages_for(int bn) { return bn == 256 ? 6 : 8; }
 constexpr int kWideStages = 4;
 
 template <int BN, bool A_MN, bool B_MN, typename OutT>
-int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp, int grid,
+int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& kp, int grid,
                cudaStream_t stream) {
   constexpr int STAGES = stages_for(BN);
   constexpr int smem = tc_smem_bytes<BN, STAGES>();
   auto kern = tc_gemm_kernel<BN, STAGES, GemmLoader<A_MN, B_MN, BN, false>, OutT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, kp);
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch");
   return CHOREO_OK;
 }
 
 template <int BN, bool A_MN, bool B_MN, typename OutT>
-int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& kp, int grid,
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const TcParams& kp, int grid,
                 cudaStream_t stream) {
   constexpr int STAGES = pair_stages_for(BN);
   constexpr int smem = tc_pair_smem_bytes<BN, STAGES>();
   auto kern = tc_gemm_pair_kernel<BN, STAGES, GemmLoader<A_MN, B_MN, BN / 2, true>, OutT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm pair)");
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, kp);
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 CTA-pair GEMM launch");
   return CHOREO_OK;
@@ -130,18 +130,18 @@ int dispatch_wide(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap
 }
 
 template <bool PAIR, int BN, typename OutT>
-int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                    const TcParams& kp, int grid, cudaStream_t s) {
   if constexpr (PAIR) {
-    if (!a_mn && !b_mn) return launch_pair<BN, false, false, OutT>(ta, tb, kp, grid, s);
-    if (!a_mn && b_mn) return launch_pair<BN, false, true, OutT>(ta, tb, kp, grid, s);
-    if (a_mn && !b_mn) return launch_pair<BN, true, false, OutT>(ta, tb, kp, grid, s);
-    return launch_pair<BN, true, true, OutT>(ta, tb, kp, grid, s);
+    if (!a_mn && !b_mn) return launch_pair<BN, false, false, OutT>(ta, tb, tc, kp, grid, s);
+    if (!a_mn && b_mn) return launch_pair<BN, false, true, OutT>(ta, tb, tc, kp, grid, s);
+    if (a_mn && !b_mn) return launch_pair<BN, true, false, OutT>(ta, tb, tc, kp, grid, s);
+    return launch_pair<BN, true, true, OutT>(ta, tb, tc, kp, grid, s);
   } else {
-    if (!a_mn && !b_mn) return launch_one<BN, false, false, OutT>(ta, tb, kp, grid, s);
-    if (!a_mn && b_mn) return launch_one<BN, false, true, OutT>(ta, tb, kp, grid, s);
-    if (a_mn && !b_mn) return launch_one<BN, true, false, OutT>(ta, tb, kp, grid, s);
-    return launch_one<BN, true, true, OutT>(ta, tb, kp, grid, s);
+    if (!a_mn && !b_mn) return launch_one<BN, false, false, OutT>(ta, tb, tc, kp, grid, s);
+    if (!a_mn && b_mn) return launch_one<BN, false, true, OutT>(ta, tb, tc, kp, grid, s);
+    if (a_mn && !b_mn) return launch_one<BN, true, false, OutT>(ta, tb, tc, kp, grid, s);
+    return launch_one<BN, true, true, OutT>(ta, tb, tc, kp, grid, s);
   }
 }
 
@@ -150,13 +150,13 @@ int dispatch_bn(const TcConfig& cfg, bool a_mn, bool b_mn, const CUtensorMap& ta
                 const CUtensorMap& tc, const TcParams& kp, int grid, cudaStream_t s) {
   if (cfg.wide) return dispatch_wide<OutT>(a_mn, b_mn, ta, tb, tc, kp, grid, s);
   if (cfg.pair) {
-    if (cfg.bn == 256) return dispatch_major<true, 256, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
-    return dispatch_major<true, 128, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
+    if (cfg.bn == 256) return dispatch_major<true, 256, OutT>(a_mn, b_mn, ta, tb, tc, kp, grid, s);
+    return dispatch_major<true, 128, OutT>(a_mn, b_mn, ta, tb, tc, kp, grid, s);
   }
   switch (cfg.bn) {
-    case 256: return dispatch_major<false, 256, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
-    case 128: return dispatch_major<false, 128, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
-    default: return dispatch_major<false, 64, OutT>(a_mn, b_mn, ta, tb, kp, grid, s);
+    case 256: return dispatch_major<false, 256, OutT>(a_mn, b_mn, ta, tb, tc, kp, grid, s);
+    case 128: return dispatch_major<false, 128, OutT>(a_mn, b_mn, ta, tb, tc, kp, grid, s);
+    default: return dispatch_major<false, 64, OutT>(a_mn, b_mn, ta, tb, tc, kp, grid, s);
   }
 }
 
@@ -168,16 +168,23 @@ TcConfig select_tc_config(int64_t m, int64_t n, int64_t k, int64_t batch, int sm
 
 TcConfig select_tile_config(int64_t m, int64_t n, int64_t k_blocks, int64_t batch, int sm_count) {
   // Candidates: wide CTA pairs (512 x 256 tiles on 2 SMs), CTA pairs
-  // (256 x BN) and single CTAs (128 x BN). Per SM a tile step computes
-  // rows_per_sm x BN outputs; `eff` is the candidate's relative tensor-pipe
-  // efficiency (shared-memory operand bandwidth per MMA and L2 traffic per
-  // FLOP favour wide tiles and pairs) and `fixed` its per-tile overhead in
-  // k-blocks (pipeline fill; for the wide tile, the half of the epilogue
-  // that is not overlapped). Time ~ waves * (k_blocks + fixed) * rows_per_sm * BN / eff.
-  struct Cand { const char* name; bool pair, wide; int bn; double eff, fixed; };
-  const Cand cands[6] = {{"wide256", true, true, 256, 1.10, 6.0},  {"pair256", true, false, 256, 1.0, 4.0},
-                         {"single256", false, false, 256, 0.97, 4.0}, {"pair128", true, false, 128, 0.92, 4.0},
-                         {"single128", false, false, 128, 0.85, 4.0}, {"single64", false, false, 64, 0.6, 4.0}};
+  // (256 x BN) and single CTAs (128 x BN). Times are in units of one k-block
+  // of MMAs over a 128 x 256 slab on one SM; a tile puts rows_per_sm x BN
+  // outputs on each SM, i.e. `area` = rows_per_sm * BN / (128 * 256) slabs.
+  // Per tile the mainloop takes (k_blocks + fixed) * area / eff (`eff`: the
+  // candidate's relative tensor-pipe efficiency — shared-memory operand
+  // bandwidth per MMA and L2 traffic per FLOP favour wide tiles and pairs;
+  // `fixed`: pipeline fill) and the epilogue epi * area (the measured time to
+  // drain, convert and store one slab). Accumulators are released to the MMA
+  // issuer as soon as they are read, so the two overlap and a tile costs the
+  // larger of them; the whole launch costs waves * that.
+  struct Cand { const char* name; bool pair, wide; int bn; double eff, fixed, epi; };
+  const Cand cands[6] = {{"wide256", true, true, 256, 1.10, 6.0, 13.8},
+                         {"pair256", true, false, 256, 1.0, 4.0, 12.8},
+                         {"single256", false, false, 256, 0.97, 4.0, 9.3},
+                         {"pair128", true, false, 128, 0.92, 4.0, 19.7},
+                         {"single128", false, false, 128, 0.85, 4.0, 11.6},
+                         {"single64", false, false, 64, 0.6, 4.0, 16.0}};
   const char* force = std::getenv("CHOREO_GEMM_TILE");  // e.g. "wide256", "single128" (tuning aid)
   double best = 1e300;
   TcConfig c{};
@@ -188,8 +195,9 @@ TcConfig select_tile_config(int64_t m, int64_t n, int64_t k_blocks, int64_t batc
     const int64_t slots = cd.pair ? sm_count / 2 : sm_count;
     const int64_t tiles = ((m + rows - 1) / rows) * ((n + cd.bn - 1) / cd.bn) * batch;
     const int64_t waves = (tiles + slots - 1) / slots;
-    const double t = static_cast<double>(waves) * (static_cast<double>(k_blocks) + cd.fixed) *
-                     static_cast<double>(rows_per_sm * cd.bn) / cd.eff;
+    const double area = static_cast<double>(rows_per_sm * cd.bn) / (kBM * 256.0);
+    const double mainloop = (static_cast<double>(k_blocks) + cd.fixed) / cd.eff;
+    const double t = static_cast<double>(waves) * area * (mainloop > cd.epi ? mainloop : cd.epi);
     if (t < best * 0.97) {
       best = t;
       c.pair = cd.pair;
@@ -273,12 +281,12 @@ int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream)
   kp.bias = p.bias;
   kp.dtype_bias = p.dtype_bias;
   kp.relu = p.relu;
-  // The wide kernel stores C through a staging tile and a TMA store when C is
-  // TMA-addressable (16-byte aligned base, leading dimension and batch stride).
+  // The kernels store C through a staging tile and bulk tensor stores when C
+  // is TMA-addressable (16-byte aligned base, leading dimension and batch stride).
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
   kp.c_tma = 0;
-  if (cfg.wide && kp.c_vec_ok) {
+  if (kp.c_vec_ok) {
     const uint64_t elem = static_cast<uint64_t>(cb);
     const uint64_t dims[3] = {static_cast<uint64_t>(p.n), static_cast<uint64_t>(p.m), static_cast<uint64_t>(p.batch)};
     const uint64_t bstride = p.batch > 1 ? static_cast<uint64_t>(p.stride_c) * elem

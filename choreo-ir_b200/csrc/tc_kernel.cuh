@@ -1,17 +1,21 @@
 // tc_kernel.cuh — the persistent, warp-specialised tcgen05 mainloop shared by
 // the GEMM and the implicit-GEMM convolution.
 //
-// CTA = 6 warps (192 threads), one CTA per SM, grid = min(tiles, SMs):
+// CTA = 10 warps (320 threads), one CTA per SM, grid = min(tiles, SMs):
 //   warp 0       TMA producer: fills a STAGES-deep ring of shared-memory
 //                stages (A tile 128 x 64, B tile BN x 64, 128-byte swizzle).
 //   warp 1       allocates 2*BN TMEM columns (two fp32 accumulators), and one
 //                elected lane issues tcgen05.mma (128 x BN x 16 per
 //                instruction, 4 per stage), releasing each stage with
 //                tcgen05.commit and signalling a finished accumulator.
-//   warps 2..5   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
-//                32*(w%4)..+31 = tile rows), apply alpha/beta/bias/ReLU, cast
-//                and store with 16-byte vector stores. Accumulators are double
-//                buffered so the epilogue of tile i overlaps the MMAs of i+1.
+//   warps 2..9   epilogue, two warps per TMEM lane quarter (warp w reads TMEM
+//                lanes 32*(w%4)..+31 = tile rows; warps 2..5 take the first
+//                half of the columns, 6..9 the second): tcgen05.ld the
+//                accumulator, hand it back to the MMA issuer, apply
+//                alpha/beta/bias/ReLU, cast, and store through a 4 KB staging
+//                buffer with bulk tensor stores (16-byte vector stores when C
+//                is not TMA-addressable). Accumulators are double buffered so
+//                the epilogue of tile i overlaps the MMAs of i+1.
 // Tiles are walked in groups of `group_m` M-tiles so concurrently running
 // CTAs share A and B panels in L2.
 //
@@ -28,7 +32,10 @@ namespace choreo_sm100 {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
+// Epilogue staging: one 4 KB buffer (32 rows x 128 bytes) per epilogue warp.
+constexpr int kStagingBytes = kEpiWarps * 4096;
 
 // Everything the kernel needs besides the two tensor maps.
 struct TcParams {
@@ -246,26 +253,76 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], OutT* cr
     if (n_base + i < p.n) crow[n_base + i] = from_f32<OutT>(v[i]);
 }
 
-// Number of 32-column TMEM chunks read per tcgen05.wait::ld in the epilogues:
-// several loads in flight hide the TMEM read latency.
-constexpr int kLdBatch = 4;
-
-// Epilogue of one warp's 32-row slab of a BN-column accumulator at TMEM
-// address `taddr`, with direct 16-byte stores (columns n0 .. n0 + BN).
-template <int BN, typename OutT>
-__device__ __forceinline__ void epilogue_slab_direct(uint32_t taddr, OutT* crow, int n0, const TcParams& p,
-                                                     bool row_ok, int lane) {
-  constexpr int kB = (BN / 32) < kLdBatch ? (BN / 32) : kLdBatch;
+// Epilogue of one warp: 32 accumulator rows (the TMEM lanes of the warp's
+// quarter) x kCols columns at TMEM address `taddr`, written to output rows
+// row0 .. row0 + 31 and columns n_first .. n_first + kCols of batch item b.
+// Columns are read from TMEM in batches of 64 (two tcgen05.ld per wait);
+// `release` hands the accumulator back to the MMA issuer right after the last
+// batch is in registers, before its arithmetic and stores, so the next tile's
+// MMAs overlap them. With a TMA-addressable C the rows leave through the
+// warp's 4 KB staging buffer as bulk tensor stores of 128-byte rows (clipped
+// by the tensor map at the matrix edges); otherwise as 16-byte vector stores.
+template <int kCols, typename OutT, typename Release>
+__device__ __forceinline__ void epilogue_warp(uint32_t taddr, int n_first, int row0, int b, const TcParams& p,
+                                              const CUtensorMap* tma_c, uint32_t stage_buf, int lane,
+                                              Release&& release) {
+  constexpr int kBatch = kCols < 64 ? kCols / 32 : 2;  // 32-column chunks per tcgen05.wait::ld
+  constexpr int kBatches = kCols / 32 / kBatch;
+  constexpr int E = 128 / static_cast<int>(sizeof(OutT));  // columns per 128-byte staging row
+  constexpr int kCpg = E / 32;                              // chunks per staging row
+  constexpr bool kTmaOk = (kBatch * 32) % E == 0;
+  // Batches holding at least one valid column, for a warp with at least one valid row.
+  int valid = 0;
+  if (row0 < p.m && n_first < p.n) {
+    valid = (p.n - n_first + kBatch * 32 - 1) / (kBatch * 32);
+    if (valid > kBatches) valid = kBatches;
+  }
+  if (valid == 0) {
+    release();
+    return;
+  }
+  const int row = row0 + lane;
+  const bool row_ok = row < p.m;
+  OutT* crow = static_cast<OutT*>(p.c) + static_cast<int64_t>(b) * p.stride_c +
+               static_cast<int64_t>(row_ok ? row : 0) * p.ldc;
+  const bool use_tma = kTmaOk && p.c_tma != 0;
 #pragma unroll 1
-  for (int c0 = 0; c0 < BN / 32; c0 += kB) {
-    if (n0 + c0 * 32 >= p.n) break;  // warp-uniform
-    uint32_t r[kB][32];
+  for (int bi = 0; bi < kBatches; ++bi) {
+    if (bi >= valid) break;  // warp-uniform
+    uint32_t r[kBatch][32];
 #pragma unroll
-    for (int j = 0; j < kB; ++j) tmem_ld_32x32b_x32(taddr + (c0 + j) * 32, r[j]);
+    for (int j = 0; j < kBatch; ++j) tmem_ld_32x32b_x32(taddr + (bi * kBatch + j) * 32, r[j]);
     tmem_wait_ld();
+    if (bi == valid - 1) release();
+    const int n_batch = n_first + bi * kBatch * 32;
+    if constexpr (kTmaOk) {
+      if (use_tma) {
 #pragma unroll
-    for (int j = 0; j < kB; ++j) {
-      const int n_base = n0 + (c0 + j) * 32;
+        for (int g = 0; g < kBatch / kCpg; ++g) {
+          const int n_base = n_batch + g * E;
+          if (n_base >= p.n) break;  // warp-uniform
+          if (lane == 0) bulk_wait_read_all();  // the warp's previous store has read the buffer
+          __syncwarp();
+#pragma unroll
+          for (int c = 0; c < kCpg; ++c) {
+            float v[32];
+            epilogue_values<OutT>(r[g * kCpg + c], v, crow, n_base + c * 32, p, row_ok, lane);
+            stage_row_32<OutT>(v, stage_buf + static_cast<uint32_t>(lane) * 128u, lane,
+                               c * (32 * static_cast<int>(sizeof(OutT)) / 16));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(tma_c, stage_buf, n_base, row0, b);
+            bulk_commit_group();
+          }
+        }
+        continue;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int n_base = n_batch + j * 32;
       if (n_base < p.n) epilogue_chunk<OutT>(r[j], crow, n_base, p, row_ok, lane);
     }
   }
@@ -285,7 +342,7 @@ struct alignas(8) TcBarriers {
 
 template <int BN, int STAGES>
 constexpr int tc_smem_bytes() {
-  return STAGES * (kBM * kBK * 2 + BN * kBK * 2) + 1024 /*alignment slack*/ +
+  return STAGES * (kBM * kBK * 2 + BN * kBK * 2) + kStagingBytes + 1024 /*alignment slack*/ +
          static_cast<int>(sizeof(TcBarriers<STAGES>));
 }
 
@@ -298,8 +355,8 @@ constexpr int tc_smem_bytes() {
 // k-block kb of batch item b into the stage at dst_a / dst_b, counted on bar.
 template <int BN, int STAGES, class Loader, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
-                   const __grid_constant__ CUtensorMap tma_b, const TcParams p) {
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                   const __grid_constant__ CUtensorMap tma_c, const TcParams p) {
   constexpr uint32_t kAStage = kBM * kBK * 2;
   constexpr uint32_t kBStage = BN * kBK * 2;
   constexpr uint32_t kStageBytes = kAStage + kBStage;
@@ -311,7 +368,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* s_a = smem;
   uint8_t* s_b = smem + STAGES * kAStage;
-  auto* bars = reinterpret_cast<TcBarriers<STAGES>*>(s_b + STAGES * kBStage);
+  uint8_t* s_stage = s_b + STAGES * kBStage;  // 1024-aligned: every stage is a multiple of 1 KB
+  auto* bars = reinterpret_cast<TcBarriers<STAGES>*>(s_stage + kStagingBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -323,8 +381,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&bars->tmem_full[i]), 1);
-      mbar_init(smem_u32(&bars->tmem_empty[i]), 4);
+      mbar_init(smem_u32(&bars->tmem_empty[i]), kEpiWarps);
     }
+    if (p.c_tma) tma_prefetch_desc(&tma_c);
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort = 0;
     fence_mbar_init();
@@ -417,7 +476,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;  // TMEM lanes this warp may read
+    const int quarter = warp & 3;       // TMEM lanes this warp may read
+    const int col_half = (warp - 2) >> 2;  // which half of the columns
+    const uint32_t stage_buf = smem_u32(s_stage) + static_cast<uint32_t>(warp - 2) * 4096u;
     uint32_t local = 0;
     for (int64_t t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
       const uint32_t buf = local & 1;
@@ -430,16 +491,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       int b, mb, nb;
       tile_coords(t, p, b, mb, nb);
-      const int row = mb * kBM + quarter * 32 + lane;
-      const bool row_ok = row < p.m;
-      OutT* crow = static_cast<OutT*>(p.c) + static_cast<int64_t>(b) * p.stride_c +
-                   static_cast<int64_t>(row_ok ? row : 0) * p.ldc;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
-      epilogue_slab_direct<BN, OutT>(taddr, crow, nb * BN, p, row_ok, lane);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bars->tmem_empty[buf]));
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN + col_half * (BN / 2);
+      epilogue_warp<BN / 2, OutT>(taddr, nb * BN + col_half * (BN / 2), mb * kBM + quarter * 32, b, p, &tma_c,
+                                  stage_buf, lane, [&] {
+                                    tc_fence_before();
+                                    __syncwarp();
+                                    if (lane == 0) mbar_arrive(smem_u32(&bars->tmem_empty[buf]));
+                                  });
     }
+    if (lane == 0) bulk_wait_all();  // staged stores finished before the CTA's shared memory goes away
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -462,17 +524,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 //     full barrier, which the leader's producer arms with both CTAs' bytes;
 //   - the leader's MMA thread releases a stage / publishes an accumulator by
 //     committing to the barrier in each CTA (two plain commits);
-//   - the leader's accumulator-empty barrier takes 8 arrivals: 4 local
-//     epilogue warps and 4 of the peer's (remote mbarrier arrive).
+//   - the leader's accumulator-empty barrier takes 16 arrivals: 8 local
+//     epilogue warps and 8 of the peer's (remote mbarrier arrive).
 template <int BN, int STAGES>
 constexpr int tc_pair_smem_bytes() {
-  return STAGES * (kBM * kBK * 2 + (BN / 2) * kBK * 2) + 1024 + static_cast<int>(sizeof(TcBarriers<STAGES>));
+  return STAGES * (kBM * kBK * 2 + (BN / 2) * kBK * 2) + kStagingBytes + 1024 +
+         static_cast<int>(sizeof(TcBarriers<STAGES>));
 }
 
 template <int BN, int STAGES, class Loader, typename OutT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
-                        const __grid_constant__ CUtensorMap tma_b, const TcParams p) {
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                        const __grid_constant__ CUtensorMap tma_c, const TcParams p) {
   constexpr int BNL = BN / 2;  // B columns this CTA stages
   constexpr uint32_t kAStage = kBM * kBK * 2;
   constexpr uint32_t kBStage = BNL * kBK * 2;
@@ -485,7 +548,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* s_a = smem;
   uint8_t* s_b = smem + STAGES * kAStage;
-  auto* bars = reinterpret_cast<TcBarriers<STAGES>*>(s_b + STAGES * kBStage);
+  uint8_t* s_stage = s_b + STAGES * kBStage;  // 1024-aligned: every stage is a multiple of 1 KB
+  auto* bars = reinterpret_cast<TcBarriers<STAGES>*>(s_stage + kStagingBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -501,8 +565,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&bars->tmem_full[i]), 1);
-      mbar_init(smem_u32(&bars->tmem_empty[i]), 8);
+      mbar_init(smem_u32(&bars->tmem_empty[i]), 2 * kEpiWarps);
     }
+    if (p.c_tma) tma_prefetch_desc(&tma_c);
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort = 0;
     fence_mbar_init();
@@ -607,6 +672,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;
+    const int col_half = (warp - 2) >> 2;
+    const uint32_t stage_buf = smem_u32(s_stage) + static_cast<uint32_t>(warp - 2) * 4096u;
     uint32_t local = 0;
     for (int64_t t = cluster_id; t < p.num_tiles; t += num_clusters, ++local) {
       const uint32_t buf = local & 1;
@@ -619,22 +686,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       int b, mb, nb;
       tile_coords(t, p, b, mb, nb);
-      const int row = mb * (2 * kBM) + static_cast<int>(rank) * kBM + quarter * 32 + lane;
-      const bool row_ok = row < p.m;
-      OutT* crow = static_cast<OutT*>(p.c) + static_cast<int64_t>(b) * p.stride_c +
-                   static_cast<int64_t>(row_ok ? row : 0) * p.ldc;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
-      epilogue_slab_direct<BN, OutT>(taddr, crow, nb * BN, p, row_ok, lane);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        const uint32_t eb = smem_u32(&bars->tmem_empty[buf]);
-        if (leader)
-          mbar_arrive(eb);
-        else
-          mbar_arrive_cluster(mapa_shared(eb, 0));
-      }
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN + col_half * (BN / 2);
+      epilogue_warp<BN / 2, OutT>(taddr, nb * BN + col_half * (BN / 2),
+                                  mb * (2 * kBM) + static_cast<int>(rank) * kBM + quarter * 32, b, p, &tma_c,
+                                  stage_buf, lane, [&] {
+                                    tc_fence_before();
+                                    __syncwarp();
+                                    if (lane == 0) {
+                                      const uint32_t eb = smem_u32(&bars->tmem_empty[buf]);
+                                      if (leader)
+                                        mbar_arrive(eb);
+                                      else
+                                        mbar_arrive_cluster(mapa_shared(eb, 0));
+                                    }
+                                  });
     }
+    if (lane == 0) bulk_wait_all();  // staged stores finished before the CTA's shared memory goes away
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -660,14 +729,11 @@ struct alignas(8) TcWideBarriers {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t tmem_full;      // this tile's accumulator is complete (leader commit, count 1)
-  uint64_t tmem_empty[2];  // accumulator half h drained by the pair's 8 epilogue warps (leader's, count 8)
+  uint64_t tmem_empty[2];  // accumulator half h read out by the pair's 16 epilogue warps (leader's, count 16)
   uint64_t drain;
   uint32_t tmem_base;
   int32_t abort;
 };
-
-// Epilogue staging: 4 warps x 2 buffers x (32 rows x 128 bytes).
-constexpr int kStagingBytes = 4 * 2 * 4096;
 
 template <int STAGES>
 constexpr int tc_wide_smem_bytes() {
@@ -710,8 +776,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     if (p.c_tma) tma_prefetch_desc(&tma_c);
     mbar_init(smem_u32(&bars->tmem_full), 1);
-    mbar_init(smem_u32(&bars->tmem_empty[0]), 8);
-    mbar_init(smem_u32(&bars->tmem_empty[1]), 8);
+    mbar_init(smem_u32(&bars->tmem_empty[0]), 2 * kEpiWarps);
+    mbar_init(smem_u32(&bars->tmem_empty[1]), 2 * kEpiWarps);
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort = 0;
     fence_mbar_init();
@@ -852,9 +918,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;
-    constexpr int E = 128 / static_cast<int>(sizeof(OutT));  // columns per 128-byte staging row
-    const uint32_t stage_base = smem_u32(s_stage) + static_cast<uint32_t>(warp - 2) * 8192u;
-    uint32_t store_iter = 0;
+    const int col_half = (warp - 2) >> 2;
+    const uint32_t stage_buf = smem_u32(s_stage) + static_cast<uint32_t>(warp - 2) * 4096u;
     uint32_t local = 0;
     for (int64_t t = cluster_id; t < p.num_tiles; t += num_clusters, ++local) {
       int ready = 0;
@@ -865,60 +930,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       int b, mb, nb;
       tile_coords(t, p, b, mb, nb);
-      for (int h = 0; h < 2; ++h) {
-        const int row0 = mb * (4 * kBM) + h * (2 * kBM) + static_cast<int>(rank) * kBM + quarter * 32;
-        const int row = row0 + lane;
-        const bool row_ok = row < p.m;
-        OutT* crow = static_cast<OutT*>(p.c) + static_cast<int64_t>(b) * p.stride_c +
-                     static_cast<int64_t>(row_ok ? row : 0) * p.ldc;
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + h * BN;
-        if (p.c_tma) {
-          // TMEM -> registers -> swizzled staging tile -> bulk tensor store (clipped at the edges).
-          if (row0 < p.m) {  // warp-uniform
-            constexpr int kCpg = E / 32;  // 32-column chunks per staging row
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN / 32; c0 += kLdBatch) {
-              if (nb * BN + c0 * 32 >= p.n) break;  // warp-uniform
-              uint32_t r[kLdBatch][32];
-#pragma unroll
-              for (int j = 0; j < kLdBatch; ++j) tmem_ld_32x32b_x32(taddr + (c0 + j) * 32, r[j]);
-              tmem_wait_ld();
-#pragma unroll
-              for (int gi = 0; gi < kLdBatch / kCpg; ++gi) {
-                const int n_base = nb * BN + c0 * 32 + gi * E;
-                if (n_base >= p.n) break;  // warp-uniform
-                const uint32_t buf = stage_base + (store_iter & 1u) * 4096u;
-                if (lane == 0) bulk_wait_read_le1();  // the store issued two groups ago has read this buffer
-                __syncwarp();
-#pragma unroll
-                for (int c = 0; c < kCpg; ++c) {
-                  float v[32];
-                  epilogue_values<OutT>(r[gi * kCpg + c], v, crow, n_base + c * 32, p, row_ok, lane);
-                  stage_row_32<OutT>(v, buf + static_cast<uint32_t>(lane) * 128u, lane,
-                                     c * (32 * static_cast<int>(sizeof(OutT)) / 16));
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                  tma_store_3d(&tma_c, buf, n_base, row0, b);
-                  bulk_commit_group();
-                }
-                ++store_iter;
-              }
-            }
-          }
-        } else {
-          epilogue_slab_direct<BN, OutT>(taddr, crow, nb * BN, p, row_ok, lane);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          const uint32_t eb = smem_u32(&bars->tmem_empty[h]);
-          if (leader)
-            mbar_arrive(eb);
-          else
-            mbar_arrive_cluster(mapa_shared(eb, 0));
-        }
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t taddr =
+            tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + h * BN + col_half * (BN / 2);
+        epilogue_warp<BN / 2, OutT>(taddr, nb * BN + col_half * (BN / 2),
+                                    mb * (4 * kBM) + h * (2 * kBM) + static_cast<int>(rank) * kBM + quarter * 32,
+                                    b, p, &tma_c, stage_buf, lane, [&] {
+                                      tc_fence_before();
+                                      __syncwarp();
+                                      if (lane == 0) {
+                                        const uint32_t eb = smem_u32(&bars->tmem_empty[h]);
+                                        if (leader)
+                                          mbar_arrive(eb);
+                                        else
+                                          mbar_arrive_cluster(mapa_shared(eb, 0));
+                                      }
+                                    });
       }
     }
     if (lane == 0) bulk_wait_all();  // staged stores finished before the CTA's shared memory goes away
