@@ -14,7 +14,8 @@ distributions; nothing is read from disk):
   custom    GEMM of --shape MxNxK and --dtype (U[-1,1], NN).
   smallk    fp16 GEMM 16384 x 16384 x 128: output-write (HBM) bound.
   conv      implicit-GEMM conv2d NHWC fp16, N=32, 56x56, C=K=256, 3x3, s1 p1,
-            activations U[0,1], weights N(0, 1/48), bias N(0, 0.1) + ReLU.
+            activations U[0,1], weights N(0, 1/48), bias N(0, 0.1) + ReLU; at
+            N > 1 the 32 images are split across the ranks (strong scaling).
   relu      elementwise ReLU over 2^28 fp16 values (HBM bound).
 One step = one launch of the path over the whole workload (per rank: its slab).
 
@@ -406,16 +407,27 @@ def setup_gemm(cb, spec, world, rank, dev, stream) -> Case:
     return case
 
 
+def conv_images(n: int, world: int, rank: int) -> tuple[int, int]:
+    """This rank's contiguous run of images (first, count): the batch split
+    evenly, the first n % world ranks taking one extra."""
+    base, extra = divmod(n, world)
+    count = base + (1 if rank < extra else 0)
+    return rank * base + min(rank, extra), count
+
+
 def setup_conv(cb, spec, world, rank, dev, stream) -> Case:
     import torch
     g = torch.Generator(device=dev)
     g.manual_seed(5 + rank)
-    x = torch.empty(spec["n"], spec["h"], spec["w"], spec["c"], device=dev).uniform_(0, 1, generator=g).half()
+    _, imgs = conv_images(spec["n"], world, rank)
+    if imgs == 0:
+        raise SystemExit(f"conv: {world} ranks for {spec['n']} images")
+    x = torch.empty(imgs, spec["h"], spec["w"], spec["c"], device=dev).uniform_(0, 1, generator=g).half()
     g.manual_seed(6)
     wt = torch.empty(spec["k"], spec["r"], spec["s"], spec["c"], device=dev).normal_(
         0, 1 / 48.0, generator=g).half()
     bias = torch.empty(spec["k"], device=dev).normal_(0, 0.1, generator=g).half()
-    out = torch.empty(spec["n"], spec["h"], spec["w"], spec["k"], device=dev, dtype=torch.float16)
+    out = torch.empty(imgs, spec["h"], spec["w"], spec["k"], device=dev, dtype=torch.float16)
     d = cb.conv_desc(x, wt, out, stride=spec["stride"], padding=spec["pad"], bias=bias, relu=spec["relu"])
     q = cb.conv2d_query(d)
     assert q.workspace_bytes == 0
@@ -434,15 +446,16 @@ def setup_conv(cb, spec, world, rank, dev, stream) -> Case:
     case.e2e_step = e2e
     case.h2d = sum(t.numel() * t.element_size() for t in (x_h, w_h, b_h))
     case.d2h = o_h.numel() * o_h.element_size()
-    case.flops, case.bytes_ = spec_flops_bytes(spec)
-    case.units_total = case.flops * world
+    case.flops, case.bytes_ = spec_flops_bytes({**spec, "n": imgs})
+    case.units_total = spec_flops_bytes(spec)[0]
     case.flush = case.bytes_ - 2.0 * out.numel() <= L2_BYTES    # activations + weights fit in L2
     case.info = {"n": spec["n"], "h": spec["h"], "w": spec["w"], "c": spec["c"], "k": spec["k"],
                  "rs": f"{spec['r']}x{spec['s']}", "stride": spec["stride"], "pad": spec["pad"],
                  "inputs": "activations U[0,1], weights N(0,1/48), bias N(0,0.1), seeded on device; "
                            "fp32 accumulation; fp16 output",
                  "epilogue": "bias+ReLU", "parallelism": "single GPU" if world == 1 else
-                 f"{world} independent replicas (no collective)",
+                 f"batch split over {world} GPUs ({imgs} images on rank {rank}), weights replicated, "
+                 "no collective",
                  "tile": f"{q.tile_m}x{q.tile_n}x{q.tile_k}", "cluster": q.cluster_m, "stages": q.stages,
                  "grid": q.grid_x}
     return case
@@ -600,7 +613,7 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
         "warmup": args.warmup,
         "ms_per_step": ms_max / args.steps,
         "higher_is_better": True,
-        "scaling": "strong" if spec.get("m_total") == 65536 and world > 1 else "weak",
+        "scaling": "strong" if world > 1 and (spec.get("m_total") == 65536 or spec["kind"] == "conv") else "weak",
         "vs_baseline": None,
         "dtype": spec["dtype"],
         "data": "synthetic",

@@ -121,3 +121,15 @@ def test_bench_workload_specs():
     assert (s["m_total"], s["n"], s["k"], s["dtype"], s["bias"], s["relu"]) == (65536, 8192, 8192, "bf16", True, True)
     g = bench.workload_spec("gemm8192", 1)
     assert (g["m_total"], g["n"], g["k"], g["dtype"]) == (8192, 8192, 8192, "f16")
+
+
+def test_bench_conv_batch_split():
+    """bench.py's conv workload splits the 32 images into contiguous runs that
+    cover the batch exactly once, sizes differing by at most one."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    for world in (1, 2, 3, 4, 5, 8):
+        runs = [bench.conv_images(32, world, r) for r in range(world)]
+        assert sum(c for _, c in runs) == 32
+        assert all(runs[i][0] + runs[i][1] == runs[i + 1][0] for i in range(world - 1))
+        assert max(c for _, c in runs) - min(c for _, c in runs) <= 1
