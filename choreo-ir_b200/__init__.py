@@ -87,6 +87,8 @@ _SIGNATURES = {
     "choreo_add": (C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
     "choreo_fill": (C.c_int, [C.c_int32, C.c_void_p, C.c_double, C.c_int64, C.c_void_p]),
     "choreo_convert": (C.c_int, [C.c_int32, C.c_void_p, C.c_int32, C.c_void_p, C.c_int64, C.c_void_p]),
+    "choreo_tensor_map_encode": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.POINTER(C.c_int64),
+                                           C.POINTER(C.c_int64), C.POINTER(C.c_uint32), C.c_int32]),
 }
 
 

@@ -390,7 +390,7 @@ int choreo_gemm_query(const choreo_gemm_desc* d, choreo_launch_config* out) {
                            : static_cast<int32_t>(std::min<int64_t>(out->tiles, sms));
   out->grid_y = 1;
   out->grid_z = 1;
-  out->block_x = 192;
+  out->block_x = kTcThreads;
   out->smem_bytes = g.cfg.smem;
   out->tmem_cols = 2 * g.cfg.bn;
   out->workspace_bytes = g.workspace;
@@ -617,6 +617,55 @@ int choreo_convert(int32_t dtype_src, const void* src, int32_t dtype_dst, void* 
   if (dtype_bytes(dtype_dst) == 0) return fail(CHOREO_ERR_UNSUPPORTED, "convert: unsupported dtype %d", dtype_dst);
   if (numel == 0) return ok();
   rc = launch_convert(dtype_src, src, dtype_dst, dst, numel, static_cast<cudaStream_t>(stream));
+  return rc ? rc : ok();
+}
+
+int choreo_tensor_map_encode(void* map, int32_t dtype, int32_t rank, const void* base, const int64_t* dims,
+                             const int64_t* strides_bytes, const uint32_t* box, int32_t swizzle_bytes) {
+  const int eb = dtype_bytes(dtype);
+  if (map == nullptr || base == nullptr || dims == nullptr || box == nullptr)
+    return fail(CHOREO_ERR_INVALID_ARG, "tensor map: null argument");
+  if ((reinterpret_cast<uintptr_t>(map) & 63u) != 0)
+    return fail(CHOREO_ERR_INVALID_ARG, "tensor map: the map must be 64-byte aligned");
+  if (eb == 0) return fail(CHOREO_ERR_UNSUPPORTED, "tensor map: unsupported dtype %d", dtype);
+  if (rank < 1 || rank > 5) return fail(CHOREO_ERR_INVALID_ARG, "tensor map: rank %d outside 1..5", rank);
+  if (rank > 1 && strides_bytes == nullptr) return fail(CHOREO_ERR_INVALID_ARG, "tensor map: null strides");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return fail(CHOREO_ERR_INVALID_ARG, "tensor map: base address is not 16-byte aligned");
+  for (int i = 0; i < rank; ++i) {
+    if (dims[i] < 1 || dims[i] > (int64_t{1} << 32))
+      return fail(CHOREO_ERR_INVALID_ARG, "tensor map: dims[%d] = %lld outside 1..2^32", i,
+                  static_cast<long long>(dims[i]));
+    if (box[i] < 1 || box[i] > 256)
+      return fail(CHOREO_ERR_INVALID_ARG, "tensor map: box[%d] = %u outside 1..256", i, box[i]);
+    if (i + 1 < rank && (strides_bytes[i] <= 0 || strides_bytes[i] % 16 != 0))
+      return fail(CHOREO_ERR_INVALID_ARG, "tensor map: strides_bytes[%d] = %lld is not a positive multiple of 16", i,
+                  static_cast<long long>(strides_bytes[i]));
+  }
+  const int64_t inner = static_cast<int64_t>(box[0]) * eb;
+  if (inner % 16 != 0)
+    return fail(CHOREO_ERR_INVALID_ARG, "tensor map: box[0] * element size = %lld bytes is not a multiple of 16",
+                static_cast<long long>(inner));
+  CUtensorMapSwizzle sw;
+  switch (swizzle_bytes) {
+    case 0: sw = CU_TENSOR_MAP_SWIZZLE_NONE; break;
+    case 32: sw = CU_TENSOR_MAP_SWIZZLE_32B; break;
+    case 64: sw = CU_TENSOR_MAP_SWIZZLE_64B; break;
+    case 128: sw = CU_TENSOR_MAP_SWIZZLE_128B; break;
+    default: return fail(CHOREO_ERR_INVALID_ARG, "tensor map: swizzle_bytes %d not 0, 32, 64 or 128", swizzle_bytes);
+  }
+  if (swizzle_bytes != 0 && inner > swizzle_bytes)
+    return fail(CHOREO_ERR_INVALID_ARG, "tensor map: a %lld-byte box row exceeds the %d-byte swizzle span",
+                static_cast<long long>(inner), swizzle_bytes);
+  const CUtensorMapDataType tdt = dtype == CHOREO_DTYPE_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                  : dtype == CHOREO_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  uint64_t d[5], st[4];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = static_cast<uint64_t>(dims[i]);
+    if (i + 1 < rank) st[i] = static_cast<uint64_t>(strides_bytes[i]);
+  }
+  int rc = encode_tmap(static_cast<CUtensorMap*>(map), tdt, rank, base, d, st, box, sw);
   return rc ? rc : ok();
 }
 

@@ -72,6 +72,7 @@ struct GemmLoader {
 
 namespace choreo_impl {
 using namespace choreo_sm100;
+static_assert(kThreads == kTcThreads, "launch width and reported block size must agree");
 
 namespace {
 

@@ -50,6 +50,10 @@ inline int group_tiles(const L2Plan& p, int tile_rows, int num_m_blocks) {
 L2Plan l2_plan();
 
 // ---------------------------------------------------------------- GEMM
+// Threads per CTA of every tcgen05 kernel (producer warp, MMA warp, 8
+// epilogue warps).
+constexpr int kTcThreads = 320;
+
 // Tile configurations of the tcgen05 GEMM (BM = 128, BK = 64).
 struct TcConfig {
   bool pair;    // CTA pair (cluster of 2, tcgen05 cta_group::2): 256-row tiles

@@ -63,7 +63,7 @@ constexpr int TILE_M = 128;            // UMMA M per CTA (TMEM lanes)
 constexpr int TILE_K = 64;             // K per pipeline stage: one 128-byte swizzle row of f16/bf16
 constexpr int UMMA_K = 16;             // K per tcgen05.mma kind::f16
 constexpr int TILE_N_CHOICES[3] = {256, 128, 64};
-constexpr int THREADS = 192;           // producer warp, MMA warp, 4 epilogue warps
+constexpr int THREADS = 320;           // producer warp, MMA warp, 8 epilogue warps
 constexpr int TMEM_COLUMNS = 512;      // per SM
 constexpr int SWIZZLE_BYTES = 128;
 constexpr int SWIZZLE_ATOM_BYTES = 1024;  // 8 rows x 128 bytes

@@ -234,6 +234,23 @@ int choreo_fill(int32_t dtype, void* dst, double value, int64_t numel, void* str
 int choreo_convert(int32_t dtype_src, const void* src, int32_t dtype_dst, void* dst,
                    int64_t numel, void* stream);
 
+/* ---- tile copies for user kernels -------------------------------------- */
+
+/* Encodes a tiled TMA tensor map (a 128-byte CUtensorMap, 64-byte aligned) for
+ * a strided 1- to 5-D f16/bf16/f32 tensor, so a user kernel can move tiles
+ * between global and shared memory with cp.async.bulk.tensor
+ * (include/choreo-ir/tensor/device_tile.hpp). Backs the TMA form of
+ * TensorView::copy_to_shared / async_copy_to_shared and of the
+ * `shared = global.tile(...)` assignment (tensor/tensor.hpp:164-254).
+ * dims and box are innermost first; strides_bytes has rank - 1 entries (the
+ * byte strides of dims 1..rank-1, each a multiple of 16); base is 16-byte
+ * aligned; box[i] in 1..256 with box[0] * element size a multiple of 16;
+ * swizzle_bytes is 0, 32, 64 or 128 (with a swizzle, box[0] * element size
+ * must not exceed it). Elements past the tensor's edge read as zero. */
+int choreo_tensor_map_encode(void* map, int32_t dtype, int32_t rank, const void* base,
+                             const int64_t* dims, const int64_t* strides_bytes,
+                             const uint32_t* box, int32_t swizzle_bytes);
+
 #ifdef __cplusplus
 }
 #endif

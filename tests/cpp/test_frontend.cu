@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "choreo-ir/choreo-ir.hpp"
+#include "choreo-ir/tensor/device_tile.hpp"
 #include "choreo-ir/utils/profiler.hpp"
 #include "mini_test.hpp"
 
@@ -492,7 +493,7 @@ TEST(gpu_auto, AnalyzeAndLaunch) {
   EXPECT_TRUE(cfg.use_tensor_cores);
   EXPECT_TRUE(cfg.tile_sizes.x == 128u || cfg.tile_sizes.x == 256u || cfg.tile_sizes.x == 512u);
   EXPECT_TRUE(cfg.cluster_m == (cfg.tile_sizes.x == 128u ? 1 : 2));
-  EXPECT_EQ(cfg.block_dim.x, 192u);
+  EXPECT_EQ(cfg.block_dim.x, 320u);
   EXPECT_GE(cfg.shared_memory, 150u * 1024u);
   EXPECT_LE(cfg.grid_dim.x, 148u);
   cfg.launch();
@@ -513,6 +514,118 @@ TEST(gpu_auto, AnalyzeAndLaunch) {
   cudaFree(d);
   EXPECT_EQ(h.back(), 5);
   finalize();
+}
+
+// -------------------------------------------------- device-side tile movement
+namespace {
+constexpr int kTR = 32, kTC = 64;
+using TileMap = device::TmaTileMap<half, kTR, kTC>;
+
+// One CTA: the tile at (row0, col0) by `shared = global.tile(...)` and by a
+// TMA tile load, both written out dense; the copied tile stored back into
+// `back` at the same place.
+__global__ void tile_move_kernel(device::GlobalMatrix<half> g, const __grid_constant__ TileMap tm, int row0,
+                                 int col0, half* out_copy, half* out_tma, device::GlobalMatrix<half> back,
+                                 int* flags) {
+  __shared__ alignas(128) half s_copy[kTR * kTC];
+  __shared__ alignas(128) half s_tma[kTR * kTC];
+  __shared__ uint64_t mbar;
+  __shared__ int issued;
+  device::SharedTile<half, kTR, kTC> a(s_copy), b(s_tma);
+  device::TileBarrier bar(&mbar);
+  if (threadIdx.x == 0) bar.init(1);
+  __syncthreads();
+  a = g.tile(row0, col0);
+  if (threadIdx.x == 0) issued = device::tma_load(tm, b, bar, row0, col0) ? 1 : 0;
+  __syncthreads();
+  const int ok = issued ? (bar.wait(0) ? 1 : 0) : 1;
+  for (int i = threadIdx.x; i < kTR * kTC; i += blockDim.x) {
+    out_copy[i] = s_copy[i];
+    out_tma[i] = issued ? s_tma[i] : __float2half(-1.0f);
+  }
+  a.store(back.tile(row0, col0));
+  if (threadIdx.x == 0) {
+    flags[0] = issued;
+    flags[1] = ok;
+  }
+}
+}  // namespace
+
+TEST(gpu_device_tile, SharedEqualsGlobalTileAndTma) {
+  initialize();
+  const int rows = 100, cols = 70, ld = 72;  // ragged matrix, 16-byte aligned rows
+  std::vector<half> h(rows * ld);
+  for (int r = 0; r < rows; ++r)
+    for (int c = 0; c < ld; ++c) h[r * ld + c] = __float2half(c < cols ? static_cast<float>((r * cols + c) % 2048) : -7.0f);
+  half *dg = nullptr, *dback = nullptr, *dcopy = nullptr, *dtma = nullptr;
+  int* dflags = nullptr;
+  cudaMalloc(&dg, h.size() * sizeof(half));
+  cudaMalloc(&dback, h.size() * sizeof(half));
+  cudaMalloc(&dcopy, kTR * kTC * sizeof(half));
+  cudaMalloc(&dtma, kTR * kTC * sizeof(half));
+  cudaMalloc(&dflags, 2 * sizeof(int));
+  cudaMemcpy(dg, h.data(), h.size() * sizeof(half), cudaMemcpyHostToDevice);
+  const device::GlobalMatrix<half> g{dg, rows, cols, ld};
+  const device::GlobalMatrix<half> back{dback, rows, cols, ld};
+  const TileMap tm = TileMap::make(g);
+  struct Case { int row0, col0; bool tma; };
+  const Case cases[] = {{0, 0, true}, {80, 40, true}, {16, 8, true}, {-8, -16, true}, {5, 3, false}, {99, 69, false}};
+  for (const Case& cs : cases) {
+    cudaMemset(dback, 0, h.size() * sizeof(half));
+    tile_move_kernel<<<1, 128>>>(g, tm, cs.row0, cs.col0, dcopy, dtma, back, dflags);
+    EXPECT_EQ(cudaDeviceSynchronize(), cudaSuccess);
+    std::vector<half> copy(kTR * kTC), tma(kTR * kTC), bk(h.size());
+    int flags[2];
+    cudaMemcpy(copy.data(), dcopy, copy.size() * sizeof(half), cudaMemcpyDeviceToHost);
+    cudaMemcpy(tma.data(), dtma, tma.size() * sizeof(half), cudaMemcpyDeviceToHost);
+    cudaMemcpy(bk.data(), dback, bk.size() * sizeof(half), cudaMemcpyDeviceToHost);
+    cudaMemcpy(flags, dflags, sizeof(flags), cudaMemcpyDeviceToHost);
+    EXPECT_EQ(flags[0], cs.tma ? 1 : 0);  // unaligned innermost coordinate: no TMA issued
+    EXPECT_EQ(flags[1], 1);
+    int bad_copy = 0, bad_tma = 0;
+    for (int r = 0; r < kTR; ++r)
+      for (int c = 0; c < kTC; ++c) {
+        const int gr = cs.row0 + r, gc = cs.col0 + c;
+        const bool in = gr >= 0 && gr < rows && gc >= 0 && gc < cols;
+        const float want = in ? static_cast<float>((gr * cols + gc) % 2048) : 0.0f;
+        if (__half2float(copy[r * kTC + c]) != want) ++bad_copy;
+        if (cs.tma && __half2float(tma[r * kTC + c]) != want) ++bad_tma;
+      }
+    EXPECT_EQ(bad_copy, 0);
+    EXPECT_EQ(bad_tma, 0);
+    int bad_back = 0;
+    for (int r = 0; r < rows; ++r)
+      for (int c = 0; c < ld; ++c) {
+        const bool in_tile = r >= cs.row0 && r < cs.row0 + kTR && c >= cs.col0 && c < cs.col0 + kTC && c < cols;
+        const float want = in_tile ? static_cast<float>((r * cols + c) % 2048) : 0.0f;
+        if (__half2float(bk[r * ld + c]) != want) ++bad_back;
+      }
+    EXPECT_EQ(bad_back, 0);
+  }
+  cudaFree(dg);
+  cudaFree(dback);
+  cudaFree(dcopy);
+  cudaFree(dtma);
+  cudaFree(dflags);
+  finalize();
+}
+
+TEST(cpu_device_tile, MapContractOnHost) {
+  // the tensor-map contract is checked before any CUDA call
+  alignas(64) unsigned char map[128];
+  const int64_t dims[2] = {70, 100}, bad_strides[1] = {140};
+  const uint32_t box[2] = {64, 32};
+  EXPECT_EQ(choreo_tensor_map_encode(map, CHOREO_DTYPE_F16, 2, reinterpret_cast<void*>(0x10000), dims, bad_strides,
+                                     box, 0),
+            CHOREO_ERR_INVALID_ARG);
+  const device::GlobalMatrix<half> g{reinterpret_cast<half*>(0x10002), 100, 70, 72};
+  bool threw = false;
+  try {
+    (void)TileMap::make(g);  // base not 16-byte aligned
+  } catch (const std::runtime_error&) {
+    threw = true;
+  }
+  EXPECT_TRUE(threw);
 }
 
 int main(int argc, char** argv) { return mini_main(argc, argv); }

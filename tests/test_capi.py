@@ -182,3 +182,34 @@ def test_rowsharded_driver_reports_failing_shard(cb):
     rc = cb.lib.choreo_gemm_rowsharded(descs, n, devices, None, None)
     assert rc == -3
     assert "shard 0 (device 999)" in cb.lib.choreo_last_error().decode()
+
+
+def test_tensor_map_encode_rejects_bad_arguments(cb):
+    """choreo_tensor_map_encode checks its contract on the host, before any
+    CUDA call: alignment of the map, base and strides, ranks, box limits and
+    the swizzle span."""
+    buf = (C.c_uint8 * 256)()
+    addr = C.addressof(buf)
+    m = addr + (-addr % 64)
+    i64 = lambda *v: (C.c_int64 * len(v))(*v)
+    u32 = lambda *v: (C.c_uint32 * len(v))(*v)
+    enc = cb.lib.choreo_tensor_map_encode
+    base = 0x10000
+    ok_dims, ok_str, ok_box = i64(72, 100), i64(144), u32(64, 32)
+    cases = [
+        ((m + 8, cb.F16, 2, base, ok_dims, ok_str, ok_box, 0), "64-byte aligned"),
+        ((m, cb.F16, 0, base, ok_dims, ok_str, ok_box, 0), "rank"),
+        ((m, cb.F16, 6, base, ok_dims, ok_str, ok_box, 0), "rank"),
+        ((m, cb.F16, 2, base + 2, ok_dims, ok_str, ok_box, 0), "16-byte aligned"),
+        ((m, cb.F16, 2, base, ok_dims, i64(140), ok_box, 0), "multiple of 16"),
+        ((m, cb.F16, 2, base, ok_dims, ok_str, u32(64, 300), 0), "outside 1..256"),
+        ((m, cb.F16, 2, base, ok_dims, ok_str, u32(12, 32), 0), "multiple of 16"),
+        ((m, cb.F16, 2, base, ok_dims, ok_str, u32(128, 8), 128), "swizzle span"),
+        ((m, cb.F16, 2, base, ok_dims, ok_str, ok_box, 48), "swizzle_bytes"),
+        ((m, cb.F16, 2, base, i64(0, 100), ok_str, ok_box, 0), "dims[0]"),
+        ((m, cb.F16, 2, None, ok_dims, ok_str, ok_box, 0), "null"),
+    ]
+    for args, msg in cases:
+        assert enc(*args) == -1, msg
+        assert msg in cb.lib.choreo_last_error().decode(), (msg, cb.lib.choreo_last_error())
+    assert enc(m, 3, 2, base, ok_dims, ok_str, ok_box, 0) == -2  # unsupported dtype

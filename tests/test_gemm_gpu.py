@@ -272,7 +272,7 @@ def test_query_reports_tcgen05_config(cb, cuda):
     import torch
     x = torch.empty(8192, 8192, device="cuda", dtype=torch.float16)
     q = cb.gemm_query(cb.make_gemm_desc(x, x, x, m=8192, n=8192, k=8192))
-    assert q.kernel == 1 and q.tile_n in (64, 128, 256) and q.block_x == 192
+    assert q.kernel == 1 and q.tile_n in (64, 128, 256) and q.block_x == 320
     assert (q.tile_m, q.cluster_m) in ((128, 1), (256, 2), (512, 2))
     assert q.grid_x <= cb.device_props(0).sm_count and q.tmem_cols == 2 * q.tile_n
     q32 = cb.gemm_query(cb.make_gemm_desc(x.float(), x.float(), x.float(), m=8192, n=8192, k=8192))
