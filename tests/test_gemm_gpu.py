@@ -315,7 +315,31 @@ def test_forced_tile_configs(cb, cuda, orc, force_tile, tile, layout, m, n, k):
     assert_close(as_f64(to_host(c), BF16), r, what=f"{tile} {layout} {m}x{n}x{k}", k=k)
 
 
-@pytest.mark.parametrize("tile", ["wide256", "pair256", "single128"])
+@pytest.mark.parametrize("tile", TILES)
+@pytest.mark.parametrize("dt_c", [F16, BF16, F32])
+def test_forced_tile_alpha_beta_bias(cb, cuda, orc, force_tile, tile, dt_c):
+    """The full epilogue (alpha * acc + beta * C + bias, ReLU) in every kernel
+    and output type, with a ragged N so the last 32-column chunk is partial
+    (bias lanes past N read nothing) and a 16-byte-aligned C so beta reads C
+    with vector loads."""
+    import torch
+    force_tile(tile)
+    m, n, k = 300, 390, 200
+    a = dev_uniform((m, k), -1, 1, 21, F16)
+    b = dev_uniform((k, n), -1, 1, 22, F16)
+    bias = dev_normal((n,), 0, 0.5, 23, BF16)
+    c0 = dev_uniform((m, 392), -1, 1, 24, dt_c)[:, :n]
+    c = c0.clone()
+    cb.gemm(a, b, c, alpha=1.5, beta=0.5, bias=bias, relu=True)
+    cb.sync_status()
+    c0h = to_host(c0.contiguous())
+    r = orc.gemm_f64(to_host(a), to_host(b), F16, alpha=1.5, beta=0.5, c0=c0h, dtype_c0=dt_c, bias=to_host(bias),
+                     dtype_bias=BF16, relu=True)
+    got = to_host(c.contiguous()).astype(np.float64) if dt_c == F32 else as_f64(to_host(c.contiguous()), dt_c)
+    assert_close(got, r, what=f"epilogue {tile} dtype {dt_c}", k=k)
+
+
+@pytest.mark.parametrize("tile", TILES)
 @pytest.mark.parametrize("dt_c", [F16, F32])
 def test_forced_tile_canary_and_batch(cb, cuda, orc, force_tile, tile, dt_c):
     """Staged (TMA-store) and direct epilogues write exactly the M x N window of
