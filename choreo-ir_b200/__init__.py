@@ -209,6 +209,62 @@ def gemm(a, b, c, *, trans_a=False, trans_b=False, alpha=1.0, beta=0.0, bias=Non
     gemm_desc(d, workspace, ws_bytes, stream)
 
 
+class HostGemmPlan:
+    """C = act(A @ B + bias) for row-major tensors in pinned HOST memory,
+    pipelined over the PCIe links: A is cut into row slabs (whole 512-row
+    tiles); the host->device copies of B, the bias and every slab of A run on
+    one copy stream, each slab's GEMM starts on the caller's stream as soon as
+    its rows have landed, and each slab of C goes back to the host on a second
+    copy stream as soon as it is computed. Device buffers and streams are
+    made once per plan and reused by every run(). run() returns with all of it
+    enqueued; the caller's stream is ordered after the last copy of C."""
+
+    def __init__(self, m, n, k, dtype, *, bias=False, relu=False, slabs=4, device=None):
+        import torch
+        self.m, self.n, self.k, self.relu = m, n, k, relu
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.a = torch.empty(m, k, device=self.device, dtype=dtype)
+        self.b = torch.empty(k, n, device=self.device, dtype=dtype)
+        self.c = torch.empty(m, n, device=self.device, dtype=dtype)
+        self.bias = torch.empty(n, device=self.device, dtype=dtype) if bias else None
+        per = -(-m // max(1, slabs))
+        per = max(512, -(-per // 512) * 512)
+        self.slabs = [(r0, min(per, m - r0)) for r0 in range(0, m, per)]
+        self.descs = [make_gemm_desc(self.a[r0:r0 + rows], self.b, self.c[r0:r0 + rows], m=rows, n=n, k=k,
+                                     bias=self.bias, relu=relu) for r0, rows in self.slabs]
+        for d in self.descs:
+            if gemm_query(d).workspace_bytes:
+                raise ValueError("HostGemmPlan: operands must be TMA-legal (16-byte aligned rows)")
+        self.s_in = torch.cuda.Stream(self.device)
+        self.s_out = torch.cuda.Stream(self.device)
+        self.ev_in = [torch.cuda.Event() for _ in self.slabs]
+        self.ev_gemm = [torch.cuda.Event() for _ in self.slabs]
+
+    def run(self, a_h, b_h, c_h, bias_h=None, stream=None):
+        import torch
+        s = torch.cuda.current_stream(self.device) if stream is None else stream
+        self.s_in.wait_stream(s)    # the previous run's GEMMs have read the device buffers
+        self.s_out.wait_stream(s)
+        with torch.cuda.stream(self.s_in):
+            self.b.copy_(b_h, non_blocking=True)
+            if self.bias is not None:
+                self.bias.copy_(bias_h, non_blocking=True)
+            for (r0, rows), ev in zip(self.slabs, self.ev_in):
+                self.a[r0:r0 + rows].copy_(a_h[r0:r0 + rows], non_blocking=True)
+                ev.record(self.s_in)
+        for (r0, rows), d, ev_in, ev_g in zip(self.slabs, self.descs, self.ev_in, self.ev_gemm):
+            s.wait_event(ev_in)
+            gemm_desc(d, stream=s)
+            ev_g.record(s)
+            self.s_out.wait_event(ev_g)
+            with torch.cuda.stream(self.s_out):
+                c_h[r0:r0 + rows].copy_(self.c[r0:r0 + rows], non_blocking=True)
+        s.wait_stream(self.s_out)
+
+    def launches(self) -> int:
+        return len(self.slabs)
+
+
 def conv_desc(x, w, out, *, stride=1, padding=1, dilation=1, bias=None, relu=False, alpha=1.0) -> ConvDesc:
     """x: NHWC, w: KRSC, out: NHWC (torch tensors, contiguous)."""
     d = ConvDesc()

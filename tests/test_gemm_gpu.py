@@ -368,3 +368,26 @@ def test_forced_tile_canary_and_batch(cb, cuda, orc, force_tile, tile, dt_c):
         r = orc.gemm_f64(to_host(ab[i]), to_host(bb[i]), F16)
         got = to_host(cbt[i]).astype(np.float64) if dt_c == F32 else as_f64(to_host(cbt[i]), dt_c)
         assert_close(got, r, what=f"batch {i} {tile}")
+
+
+def test_host_gemm_plan_pipelined(cb, cuda, orc):
+    """HostGemmPlan: pinned host A/B/bias in, C out, row slabs overlapped on
+    three streams (a ragged last slab included); two runs on the same plan,
+    the second with new inputs, each checked against fp64."""
+    import torch
+    m, n, k = 1500, 384, 256
+    plan = cb.HostGemmPlan(m, n, k, torch.bfloat16, bias=True, relu=True, slabs=3)
+    assert [rows for _, rows in plan.slabs] == [512, 512, 476]
+    for seed in (31, 41):
+        a = torch.empty(m, k).uniform_(-1, 1, generator=torch.Generator().manual_seed(seed)).bfloat16().pin_memory()
+        b = torch.empty(k, n).uniform_(-1, 1, generator=torch.Generator().manual_seed(seed + 1)).bfloat16().pin_memory()
+        bias = torch.empty(n).normal_(0, 0.3, generator=torch.Generator().manual_seed(seed + 2)).bfloat16().pin_memory()
+        c = torch.full((m, n), 7.0, dtype=torch.bfloat16).pin_memory()
+        plan.run(a, b, c, bias)
+        torch.cuda.current_stream().synchronize()
+        cb.sync_status()
+        ah, bh = a.view(torch.int16).numpy().view(np.uint16), b.view(torch.int16).numpy().view(np.uint16)
+        biash = bias.view(torch.int16).numpy().view(np.uint16)
+        r = orc.gemm_f64(ah, bh, BF16, bias=biash, dtype_bias=BF16, relu=True)
+        got = as_f64(c.view(torch.int16).numpy().view(np.uint16), BF16)
+        assert_close(got, r, what=f"host plan seed {seed}", k=k)
