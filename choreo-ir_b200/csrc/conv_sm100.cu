@@ -63,6 +63,12 @@ struct ConvLoader {
     else
       tma_load_3d(dst_b, tb, bar, cb * 64, rs, n0, pol_b);
   }
+  // The wide tile's 256 rows of one CTA: two 128-pixel im2col loads.
+  __device__ __forceinline__ static void issue_a_256(const CUtensorMap* ta, const TcParams& p, int b, int m0,
+                                                     int kb, uint32_t dst_a, uint32_t bar, uint64_t pol_a) {
+    issue_a(ta, p, b, m0, kb, dst_a, bar, pol_a);
+    issue_a(ta, p, b, m0 + 128, kb, dst_a + 16384, bar, pol_a);
+  }
   __device__ __forceinline__ static void issue(const CUtensorMap* ta, const CUtensorMap* tb,
                                                const TcParams& p, int b, int m0, int n0, int kb,
                                                uint32_t dst_a, uint32_t dst_b, uint32_t bar,

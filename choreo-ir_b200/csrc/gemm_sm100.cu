@@ -48,6 +48,18 @@ struct GemmLoader {
       load3<PAIR>(dst_a + 8192, ta, bar, m0 + 64, k0, b, pol_a);
     }
   }
+  // A rows [m0, m0 + 256) of k-block kb (the wide tile's two halves of one
+  // CTA): one 256-row box when K-major, four 64-row chunks when MN-major.
+  __device__ __forceinline__ static void issue_a_256(const CUtensorMap* ta, const TcParams&, int b, int m0, int kb,
+                                                     uint32_t dst_a, uint32_t bar, uint64_t pol_a) {
+    const int k0 = kb * kBK;
+    if constexpr (!A_MN) {
+      load3<PAIR>(dst_a, ta, bar, k0, m0, b, pol_a);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) load3<PAIR>(dst_a + j * 8192, ta, bar, m0 + j * 64, k0, b, pol_a);
+    }
+  }
   // B columns [n0, n0 + BNL) of k-block kb.
   __device__ __forceinline__ static void issue_b(const CUtensorMap* tb, const TcParams&, int b, int n0, int kb,
                                                  uint32_t dst_b, uint32_t bar, uint64_t pol_b) {
@@ -239,7 +251,7 @@ int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream)
     const uint64_t dims[3] = {inner, outer, static_cast<uint64_t>(p.batch)};
     const uint64_t bstride = p.batch > 1 ? p.stride_a * 2 : outer * p.lda * 2;
     const uint64_t strides[2] = {static_cast<uint64_t>(p.lda) * 2, bstride};
-    const uint32_t box[3] = {64, p.a_mn ? 64u : 128u, 1};
+    const uint32_t box[3] = {64, p.a_mn ? 64u : (cfg.wide ? 256u : 128u), 1};
     int rc = encode_tmap(&ta, tdt, 3, p.a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }

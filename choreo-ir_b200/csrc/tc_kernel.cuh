@@ -804,7 +804,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int64_t t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
         int b, mb, nb;
         tile_coords(t, p, b, mb, nb);
-        const int m0 = mb * (4 * kBM) + static_cast<int>(rank) * kBM;
+        const int m0 = mb * (4 * kBM) + static_cast<int>(rank) * (2 * kBM);  // this CTA's 256 rows
         const int n0 = nb * BN + static_cast<int>(rank) * BNL;
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
           if (!mbar_wait(smem_u32(&bars->empty[stage]), phase ^ 1, wctx, kStatusTimeoutProducer)) {
@@ -815,8 +815,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (leader) mbar_arrive_expect_tx(own_full, 2 * kStageBytes);
           const uint32_t bar = mapa_shared(own_full, 0);
           const uint32_t a_dst = smem_u32(s_a + stage * kAStage);
-          Loader::issue_a(&tma_a, p, b, m0, kb, a_dst, bar, pol_a);
-          Loader::issue_a(&tma_a, p, b, m0 + 2 * kBM, kb, a_dst + kAHalf, bar, pol_a);
+          Loader::issue_a_256(&tma_a, p, b, m0, kb, a_dst, bar, pol_a);
           Loader::issue_b(&tma_b, p, b, n0, kb, smem_u32(s_b + stage * kBStage), bar, pol_b);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -935,7 +934,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const uint32_t taddr =
             tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + h * BN + col_half * (BN / 2);
         epilogue_warp<BN / 2, OutT>(taddr, nb * BN + col_half * (BN / 2),
-                                    mb * (4 * kBM) + h * (2 * kBM) + static_cast<int>(rank) * kBM + quarter * 32,
+                                    mb * (4 * kBM) + static_cast<int>(rank) * (2 * kBM) + h * kBM + quarter * 32,
                                     b, p, &tma_c, stage_buf, lane, [&] {
                                       tc_fence_before();
                                       __syncwarp();
