@@ -381,7 +381,7 @@ def setup_gemm(cb, spec, world, rank, dev, stream) -> Case:
     a_h, b_h = _pinned_copy(a), _pinned_copy(b)
     bias_h = _pinned_copy(bias) if bias is not None else None
     c_h = torch.empty(rows, N, dtype=dt, pin_memory=True)
-    plan = cb.HostGemmPlan(rows, N, K, dt, bias=bias is not None, relu=spec["relu"], slabs=4, device=dev)
+    plan = cb.HostGemmPlan(rows, N, K, dt, bias=bias is not None, relu=spec["relu"], device=dev)
     case.e2e_step = lambda: plan.run(a_h, b_h, c_h, bias_h, stream=stream)
     case.h2d = sum(t.numel() * t.element_size() for t in (a_h, b_h, bias_h) if t is not None)
     case.d2h = c_h.numel() * c_h.element_size()

@@ -42,7 +42,8 @@ class LaunchConfig(C.Structure):
         ("stages", C.c_int32), ("cluster_m", C.c_int32),
         ("grid_x", C.c_int32), ("grid_y", C.c_int32), ("grid_z", C.c_int32),
         ("block_x", C.c_int32), ("smem_bytes", C.c_int32), ("tmem_cols", C.c_int32),
-        ("tiles", C.c_int64), ("workspace_bytes", C.c_int64),
+        ("tiles", C.c_int64), ("workspace_bytes", C.c_int64), ("workspace_min_bytes", C.c_int64),
+        ("split_k", C.c_int64),
     ]
 
 
@@ -219,7 +220,7 @@ class HostGemmPlan:
     made once per plan and reused by every run(). run() returns with all of it
     enqueued; the caller's stream is ordered after the last copy of C."""
 
-    def __init__(self, m, n, k, dtype, *, bias=False, relu=False, slabs=4, device=None):
+    def __init__(self, m, n, k, dtype, *, bias=False, relu=False, slabs=None, device=None):
         import torch
         self.m, self.n, self.k, self.relu = m, n, k, relu
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
@@ -227,13 +228,15 @@ class HostGemmPlan:
         self.b = torch.empty(k, n, device=self.device, dtype=dtype)
         self.c = torch.empty(m, n, device=self.device, dtype=dtype)
         self.bias = torch.empty(n, device=self.device, dtype=dtype) if bias else None
+        if slabs is None:  # ~1024-row slabs, at most 16: the last slab's GEMM and copy-out are the exposed tail
+            slabs = max(1, min(16, m // 1024))
         per = -(-m // max(1, slabs))
         per = max(512, -(-per // 512) * 512)
         self.slabs = [(r0, min(per, m - r0)) for r0 in range(0, m, per)]
         self.descs = [make_gemm_desc(self.a[r0:r0 + rows], self.b, self.c[r0:r0 + rows], m=rows, n=n, k=k,
                                      bias=self.bias, relu=relu) for r0, rows in self.slabs]
         for d in self.descs:
-            if gemm_query(d).workspace_bytes:
+            if gemm_query(d).workspace_min_bytes:
                 raise ValueError("HostGemmPlan: operands must be TMA-legal (16-byte aligned rows)")
         self.s_in = torch.cuda.Stream(self.device)
         self.s_out = torch.cuda.Stream(self.device)

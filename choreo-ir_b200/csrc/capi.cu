@@ -297,9 +297,39 @@ OperandPlan plan_operand(const void* ptr, int64_t ld, int64_t stride, int64_t ba
 
 struct GemmPlan {
   OperandPlan a, b;
-  int64_t workspace = 0;
+  int64_t workspace = 0;    // required: operand repacks
   TcConfig cfg{};
+  // The fastest plan may cut K into `split` ranges computed in parallel
+  // (split_cfg) and summed by a second pass; it needs split_bytes of fp32
+  // partials in the workspace and runs only when the caller provides them.
+  int64_t split = 1;
+  TcConfig split_cfg{};
+  int64_t split_bytes = 0;
 };
+
+int64_t tile_count(const TcConfig& c, int64_t m, int64_t n, int64_t items) {
+  const int64_t rows = tile_rows_of(c);
+  return ((m + rows - 1) / rows) * ((n + c.bn - 1) / c.bn) * items;
+}
+
+// Split K when the output has so few tiles that most SMs would idle through a
+// long reduction: the largest number of equal k-block ranges (at least 16
+// k-blocks = 1024 of K each) whose tiles still fit in one wave.
+void choose_split(const choreo_gemm_desc& d, GemmPlan& g, int sms) {
+  if (d.batch != 1) return;
+  const int64_t kb = (d.k + 63) / 64;
+  const int64_t slots = g.cfg.pair ? sms / 2 : sms;
+  if (kb < 32 || tile_count(g.cfg, d.m, d.n, 1) * 2 > slots) return;
+  for (int64_t s = 2; s <= 64 && kb / s >= 16; ++s) {
+    if (kb % s != 0) continue;
+    const TcConfig c = select_tile_config(d.m, d.n, kb / s, s, sms);
+    const int64_t slots_c = c.pair ? sms / 2 : sms;
+    if (tile_count(c, d.m, d.n, s) > slots_c) continue;
+    g.split = s;
+    g.split_cfg = c;
+  }
+  if (g.split > 1) g.split_bytes = round_up(g.split * d.m * d.n * 4, 256);
+}
 
 GemmPlan plan_tc(const choreo_gemm_desc& d) {
   GemmPlan g;
@@ -308,7 +338,9 @@ GemmPlan plan_tc(const choreo_gemm_desc& d) {
   g.a.offset = 0;
   g.b.offset = g.a.bytes;
   g.workspace = g.a.bytes + g.b.bytes;
-  g.cfg = select_tc_config(d.m, d.n, d.k, d.batch, current_sm_count());
+  const int sms = current_sm_count();
+  g.cfg = select_tc_config(d.m, d.n, d.k, d.batch, sms);
+  choose_split(d, g, sms);
   return g;
 }
 
@@ -377,25 +409,28 @@ int choreo_gemm_query(const choreo_gemm_desc* d, choreo_launch_config* out) {
     out->block_x = 256;
     out->smem_bytes = 2 * 16 * 68 * 4;
     out->tiles = static_cast<int64_t>(out->grid_x) * out->grid_y * out->grid_z;
+    out->split_k = 1;
     return ok();
   }
   GemmPlan g = plan_tc(*d);
-  const int64_t rows = tile_rows_of(g.cfg);
+  const TcConfig& c = g.split > 1 ? g.split_cfg : g.cfg;
   out->kernel = 1;
-  out->tile_m = static_cast<int32_t>(rows);
-  out->tile_n = g.cfg.bn;
+  out->tile_m = static_cast<int32_t>(tile_rows_of(c));
+  out->tile_n = c.bn;
   out->tile_k = 64;
-  out->stages = g.cfg.stages;
-  out->cluster_m = g.cfg.pair ? 2 : 1;
-  out->tiles = ((d->m + rows - 1) / rows) * ((d->n + g.cfg.bn - 1) / g.cfg.bn) * d->batch;
-  out->grid_x = g.cfg.pair ? 2 * static_cast<int32_t>(std::min<int64_t>(out->tiles, sms / 2))
-                           : static_cast<int32_t>(std::min<int64_t>(out->tiles, sms));
+  out->stages = c.stages;
+  out->cluster_m = c.pair ? 2 : 1;
+  out->tiles = tile_count(c, d->m, d->n, g.split > 1 ? g.split : d->batch);
+  out->grid_x = c.pair ? 2 * static_cast<int32_t>(std::min<int64_t>(out->tiles, sms / 2))
+                       : static_cast<int32_t>(std::min<int64_t>(out->tiles, sms));
   out->grid_y = 1;
   out->grid_z = 1;
   out->block_x = kTcThreads;
-  out->smem_bytes = g.cfg.smem;
-  out->tmem_cols = 2 * g.cfg.bn;
-  out->workspace_bytes = g.workspace;
+  out->smem_bytes = c.smem;
+  out->tmem_cols = 2 * c.bn;
+  out->workspace_bytes = g.workspace + g.split_bytes;
+  out->workspace_min_bytes = g.workspace;
+  out->split_k = g.split;
   return ok();
 }
 
@@ -414,6 +449,11 @@ int choreo_gemm(const choreo_gemm_desc* d, void* workspace, size_t workspace_byt
                   "GEMM: an operand is not 16-byte aligned (base, leading dimension or batch stride); "
                   "it is repacked into a workspace of %lld bytes, got %zu",
                   (long long)g.workspace, workspace_bytes);
+  }
+  // The K split runs only when the caller's workspace also holds its partials.
+  const bool split = g.split > 1 && workspace != nullptr &&
+                     workspace_bytes >= static_cast<size_t>(g.workspace + g.split_bytes);
+  if (g.workspace > 0 || split) {
     if ((rc = check_device_ptr(workspace, "GEMM workspace"))) return rc;
     if (reinterpret_cast<uintptr_t>(workspace) & 255u)
       return fail(CHOREO_ERR_WORKSPACE, "GEMM: workspace must be 256-byte aligned");
@@ -449,6 +489,24 @@ int choreo_gemm(const choreo_gemm_desc* d, void* workspace, size_t workspace_byt
     p.b = dst;
     p.ldb = g.b.ld_pad;
     p.stride_b = g.b.outer * g.b.ld_pad;
+  }
+  if (split) {
+    // First pass: fp32 partials [split][m][n] after the repacked operands.
+    float* partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + g.workspace);
+    p.split = g.split;
+    p.c = partials;
+    p.ldc = d->n;
+    p.stride_c = d->m * d->n;
+    p.dtype_c = CHOREO_DTYPE_F32;
+    p.alpha = 1.f;
+    p.beta = 0.f;
+    p.bias = nullptr;
+    p.dtype_bias = CHOREO_DTYPE_F32;
+    p.relu = 0;
+    if ((rc = launch_gemm_tc(p, g.split_cfg, s))) return rc;
+    rc = launch_splitk_reduce(partials, g.split, d->m, d->n, d->c, d->ldc, d->dtype_c, d->alpha, d->beta, d->bias,
+                              d->dtype_bias, d->relu, s);
+    return rc ? rc : ok();
   }
   p.c = d->c;
   p.ldc = d->ldc;

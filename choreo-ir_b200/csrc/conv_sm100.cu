@@ -196,6 +196,8 @@ int conv_query(const choreo_conv_desc& d, choreo_launch_config* out) {
   out->smem_bytes = c.smem;
   out->tmem_cols = 2 * c.bn;
   out->workspace_bytes = 0;
+  out->workspace_min_bytes = 0;
+  out->split_k = 1;
   return CHOREO_OK;
 }
 

@@ -37,10 +37,17 @@ template <bool A_MN, bool B_MN, int BNL, bool PAIR>
 struct GemmLoader {
   static constexpr bool kAMn = A_MN;
   static constexpr bool kBMn = B_MN;
+  // With a K split (p.split_kb > 0) the batch index b selects k-blocks
+  // [b * split_kb, (b + 1) * split_kb) of the single operand pair.
+  __device__ __forceinline__ static int k_origin(const TcParams& p, int b, int kb) {
+    return (p.split_kb > 0 ? b * p.split_kb + kb : kb) * kBK;
+  }
+  __device__ __forceinline__ static int batch_of(const TcParams& p, int b) { return p.split_kb > 0 ? 0 : b; }
   // A rows [m0, m0 + 128) of k-block kb.
-  __device__ __forceinline__ static void issue_a(const CUtensorMap* ta, const TcParams&, int b, int m0, int kb,
+  __device__ __forceinline__ static void issue_a(const CUtensorMap* ta, const TcParams& p, int b0, int m0, int kb,
                                                  uint32_t dst_a, uint32_t bar, uint64_t pol_a) {
-    const int k0 = kb * kBK;
+    const int k0 = k_origin(p, b0, kb);
+    const int b = batch_of(p, b0);
     if constexpr (!A_MN) {
       load3<PAIR>(dst_a, ta, bar, k0, m0, b, pol_a);
     } else {
@@ -50,9 +57,10 @@ struct GemmLoader {
   }
   // A rows [m0, m0 + 256) of k-block kb (the wide tile's two halves of one
   // CTA): one 256-row box when K-major, four 64-row chunks when MN-major.
-  __device__ __forceinline__ static void issue_a_256(const CUtensorMap* ta, const TcParams&, int b, int m0, int kb,
-                                                     uint32_t dst_a, uint32_t bar, uint64_t pol_a) {
-    const int k0 = kb * kBK;
+  __device__ __forceinline__ static void issue_a_256(const CUtensorMap* ta, const TcParams& p, int b0, int m0,
+                                                     int kb, uint32_t dst_a, uint32_t bar, uint64_t pol_a) {
+    const int k0 = k_origin(p, b0, kb);
+    const int b = batch_of(p, b0);
     if constexpr (!A_MN) {
       load3<PAIR>(dst_a, ta, bar, k0, m0, b, pol_a);
     } else {
@@ -61,9 +69,10 @@ struct GemmLoader {
     }
   }
   // B columns [n0, n0 + BNL) of k-block kb.
-  __device__ __forceinline__ static void issue_b(const CUtensorMap* tb, const TcParams&, int b, int n0, int kb,
+  __device__ __forceinline__ static void issue_b(const CUtensorMap* tb, const TcParams& p, int b0, int n0, int kb,
                                                  uint32_t dst_b, uint32_t bar, uint64_t pol_b) {
-    const int k0 = kb * kBK;
+    const int k0 = k_origin(p, b0, kb);
+    const int b = batch_of(p, b0);
     if constexpr (!B_MN) {
       load3<PAIR>(dst_b, tb, bar, k0, n0, b, pol_b);
     } else {
@@ -270,12 +279,18 @@ int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream)
   TcParams kp{};
   kp.m = static_cast<int32_t>(p.m);
   kp.n = static_cast<int32_t>(p.n);
-  kp.num_k_blocks = static_cast<int32_t>((p.k + kBK - 1) / kBK);
+  const int64_t kblocks = (p.k + kBK - 1) / kBK;
+  const int64_t items = p.split > 1 ? p.split : p.batch;  // scheduler batch: K splits or batch items
+  if (p.split > 1 && (p.batch != 1 || kblocks % p.split != 0))
+    return fail(CHOREO_ERR_INVALID_ARG, "split-K launch: batch %lld, %lld k-blocks over %lld splits",
+                (long long)p.batch, (long long)kblocks, (long long)p.split);
+  kp.num_k_blocks = static_cast<int32_t>(kblocks / (p.split > 1 ? p.split : 1));
+  kp.split_kb = p.split > 1 ? kp.num_k_blocks : 0;
   const int64_t tile_rows = tile_rows_of(cfg);
   kp.num_m_blocks = static_cast<int32_t>((p.m + tile_rows - 1) / tile_rows);
   kp.num_n_blocks = static_cast<int32_t>((p.n + cfg.bn - 1) / cfg.bn);
-  kp.batch = static_cast<int32_t>(p.batch);
-  kp.num_tiles = static_cast<int64_t>(kp.num_m_blocks) * kp.num_n_blocks * p.batch;
+  kp.batch = static_cast<int32_t>(items);
+  kp.num_tiles = static_cast<int64_t>(kp.num_m_blocks) * kp.num_n_blocks * items;
   const L2Plan l2 = l2_plan();
   kp.group_m = group_tiles(l2, static_cast<int>(tile_rows), kp.num_m_blocks);
   kp.l2_policy_a = l2.policy_a;
@@ -286,7 +301,7 @@ int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream)
   kp.stride_c = p.stride_c;
   const int cb = dtype_bytes(p.dtype_c);
   kp.c_vec_ok = ((reinterpret_cast<uintptr_t>(p.c) & 15u) == 0 && (p.ldc * cb) % 16 == 0 &&
-                 (p.batch == 1 || (p.stride_c * cb) % 16 == 0))
+                 (items == 1 || (p.stride_c * cb) % 16 == 0))
                     ? 1
                     : 0;
   kp.alpha = p.alpha;
@@ -301,8 +316,8 @@ int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream)
   kp.c_tma = 0;
   if (kp.c_vec_ok) {
     const uint64_t elem = static_cast<uint64_t>(cb);
-    const uint64_t dims[3] = {static_cast<uint64_t>(p.n), static_cast<uint64_t>(p.m), static_cast<uint64_t>(p.batch)};
-    const uint64_t bstride = p.batch > 1 ? static_cast<uint64_t>(p.stride_c) * elem
+    const uint64_t dims[3] = {static_cast<uint64_t>(p.n), static_cast<uint64_t>(p.m), static_cast<uint64_t>(items)};
+    const uint64_t bstride = items > 1 ? static_cast<uint64_t>(p.stride_c) * elem
                                          : static_cast<uint64_t>(p.m) * static_cast<uint64_t>(p.ldc) * elem;
     const uint64_t strides[2] = {static_cast<uint64_t>(p.ldc) * elem, bstride};
     const uint32_t box[3] = {static_cast<uint32_t>(128 / elem), 32, 1};

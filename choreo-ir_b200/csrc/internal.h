@@ -79,8 +79,18 @@ struct TcProblem {
   float alpha, beta;
   const void* bias; int dtype_bias;
   int relu;
+  // > 1: K is cut into `split` equal ranges of whole k-blocks, computed as the
+  // batch items of one launch (batch must be 1); C is then the fp32 partial
+  // buffer [split][m][n] and the epilogue fields must be the identity.
+  int64_t split = 1;
 };
 int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream);
+
+// Sums `split` fp32 partials [split][m][n] and applies the epilogue
+// (alpha, beta * C, bias, ReLU, cast) into C.
+int launch_splitk_reduce(const float* partials, int64_t split, int64_t m, int64_t n, void* c, int64_t ldc,
+                         int dtype_c, float alpha, float beta, const void* bias, int dtype_bias, int relu,
+                         cudaStream_t stream);
 
 // CUDA-core f32 GEMM (A/B/C f32), any strides.
 int launch_gemm_f32(const choreo_gemm_desc& d, cudaStream_t stream);

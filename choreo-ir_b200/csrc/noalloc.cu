@@ -71,12 +71,12 @@ extern "C" int choreo_gemm_noalloc(const choreo_gemm_desc* d, void* stream) {
   choreo_launch_config q;
   int rc = choreo_gemm_query(d, &q);
   if (rc) return rc;
-  if (q.workspace_bytes > static_cast<int64_t>(CHOREO_GEMM_NOALLOC_SCRATCH_BYTES))
+  if (q.workspace_min_bytes > static_cast<int64_t>(CHOREO_GEMM_NOALLOC_SCRATCH_BYTES))
     return choreo_impl::fail(CHOREO_ERR_WORKSPACE,
                              "GEMM (no-alloc): repacking the unaligned operands needs %lld bytes of scratch; "
                              "the built-in scratch holds %u bytes. Align the operands (16-byte base and "
                              "leading dimension) or use choreo_gemm with a workspace.",
-                             static_cast<long long>(q.workspace_bytes), CHOREO_GEMM_NOALLOC_SCRATCH_BYTES);
+                             static_cast<long long>(q.workspace_min_bytes), CHOREO_GEMM_NOALLOC_SCRATCH_BYTES);
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
   if (q.workspace_bytes > 0) {

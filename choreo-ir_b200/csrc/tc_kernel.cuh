@@ -40,7 +40,8 @@ constexpr int kStagingBytes = kEpiWarps * 4096;
 // Everything the kernel needs besides the two tensor maps.
 struct TcParams {
   int32_t m, n;            // output rows / columns (per batch item)
-  int32_t num_k_blocks;    // K / 64 rounded up (conv: R*S*ceil(C/64))
+  int32_t num_k_blocks;    // K / 64 rounded up (conv: R*S*ceil(C/64)); per split when split_kb > 0
+  int32_t split_kb;        // > 0: the batch index is a K split of split_kb k-blocks (GEMM loader)
   int32_t num_m_blocks, num_n_blocks;
   int32_t batch;
   int64_t num_tiles;

@@ -40,7 +40,8 @@ class LaunchConfig {
   int stages = 0;
   int cluster_m = 1;
   int64_t tiles = 0;
-  size_t workspace_bytes = 0;
+  size_t workspace_bytes = 0;  // scratch of the fastest plan (K-split partials, repacks)
+  int split_k = 1;             // K ranges computed in parallel and summed in fp32
   bool use_tensor_cores = false;
   cudaStream_t stream = nullptr;
 
@@ -112,6 +113,7 @@ LaunchConfig auto_analyze(const Tensor<T>& A, const Tensor<T>& B, const Tensor<T
   lc.cluster_m = q.cluster_m;
   lc.tiles = q.tiles;
   lc.workspace_bytes = static_cast<size_t>(q.workspace_bytes);
+  lc.split_k = static_cast<int>(q.split_k);
   lc.use_tensor_cores = q.kernel == 1;
   lc.stream = stream;
   return lc;

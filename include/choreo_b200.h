@@ -93,8 +93,12 @@ typedef struct choreo_launch_config {
   int32_t block_x;         /* threads per CTA */
   int32_t smem_bytes;      /* dynamic shared memory per CTA */
   int32_t tmem_cols;       /* tensor-memory columns per CTA */
-  int64_t tiles;           /* output tiles (all batch items) */
-  int64_t workspace_bytes; /* device scratch the call needs (0 = none) */
+  int64_t tiles;           /* output tiles (all batch items, all K splits) */
+  int64_t workspace_bytes; /* device scratch for the fastest plan (0 = none) */
+  int64_t workspace_min_bytes; /* scratch the call cannot run without (operand repacks);
+                                  between this and workspace_bytes the call runs without
+                                  splitting K */
+  int64_t split_k;         /* K ranges computed in parallel and summed in fp32 (1 = none) */
 } choreo_launch_config;
 
 /* Implicit-GEMM 2-D convolution, NHWC activations, KRSC weights:

@@ -391,3 +391,84 @@ def test_host_gemm_plan_pipelined(cb, cuda, orc):
         r = orc.gemm_f64(ah, bh, BF16, bias=biash, dtype_bias=BF16, relu=True)
         got = as_f64(c.view(torch.int16).numpy().view(np.uint16), BF16)
         assert_close(got, r, what=f"host plan seed {seed}", k=k)
+
+
+def test_nonfinite_inputs_propagate(cb, cuda, orc):
+    """A NaN or an Inf in A reaches every element of its output row the way
+    fp64 arithmetic says (the tensor cores do not flush or saturate them)."""
+    import torch
+    m, n, k = 300, 260, 192
+    a = orc.to_bits(orc.uniform((m, k), -1, 1, 51), F16)
+    b = orc.to_bits(orc.uniform((k, n), 0.25, 1, 52), F16)  # positive B: Inf * b stays +Inf
+    a[7, 13] = 0x7E00      # NaN
+    a[100, 5] = 0x7C00     # +Inf
+    a[250, 0] = 0xFC00     # -Inf
+    c = run(cb, to_dev(a, F16), to_dev(b, F16), m, n, k, F16, F32)
+    got = to_host(c).astype(np.float64)
+    assert np.isnan(got[7]).all()
+    assert np.isposinf(got[100]).all() and np.isneginf(got[250]).all()
+    rest = np.setdiff1d(np.arange(m), [7, 100, 250])
+    r = orc.gemm_f64(a, b, F16, rows=rest)
+    assert np.isfinite(got[rest]).all()
+    assert_close(got[rest], r, what="finite rows", k=k)
+
+
+def test_long_reduction(cb, cuda, orc):
+    """K = 65536 (1024 k-blocks through the pipeline). The tensor cores'
+    fp32 accumulation error grows about linearly with K here (it is no longer
+    within the sqrt(K)-scaled per-element floor), so the check is the one that
+    holds for any tensor-core GEMM: normwise error <= 1e-3 against fp64, and a
+    largest absolute error no worse than cuBLAS's on the same inputs with fp32
+    output (+25 %)."""
+    import torch
+    m, n, k = 256, 512, 65536
+    a = orc.to_bits(orc.uniform((m, k), -1, 1, 53), F16)
+    b = orc.to_bits(orc.uniform((k, n), -1, 1, 54), F16)
+    ad, bd = to_dev(a, F16), to_dev(b, F16)
+    c = run(cb, ad, bd, m, n, k, F16, F32)
+    r = orc.gemm_f64(a, b, F16)
+    got = to_host(c).astype(np.float64)
+    assert np.isfinite(got).all()
+    assert orc.normwise_err(got, r) <= 1e-3
+    e_ours = float(np.max(np.abs(got - r)))
+    try:
+        ref = torch.mm(ad, bd, out_dtype=torch.float32)
+    except (RuntimeError, TypeError):
+        pytest.skip("torch.mm(out_dtype=float32) unavailable: cuBLAS side check skipped")
+    e_cublas = float(np.max(np.abs(ref.cpu().double().numpy() - r)))
+    rms = float(np.sqrt(np.mean(r * r)))
+    print(f"K=65536 max |error|: choreo {e_ours:.3e}, cuBLAS {e_cublas:.3e}; rms {rms:.1f}")
+    assert e_ours <= 1.25 * e_cublas + 1e-6 * rms, (e_ours, e_cublas, rms)
+
+
+@pytest.mark.parametrize("layout", ["NN", "NT", "TN"])
+@pytest.mark.parametrize("dt_c", [F16, BF16, F32])
+def test_split_k(cb, cuda, orc, layout, dt_c):
+    """Few output tiles over a long K: the query plans K splits (fp32 partials
+    in the workspace, summed by a second pass that applies the epilogue). The
+    split result and the unsplit one (no workspace given) both match fp64,
+    with alpha, beta, bias and ReLU."""
+    import torch
+    m, n, k = 300, 200, 8192
+    ta, tb = layout[0] == "T", layout[1] == "T"
+    a = dev_uniform((k, m) if ta else (m, k), -1, 1, 61, F16)
+    b = dev_uniform((n, k) if tb else (k, n), -1, 1, 62, F16)
+    bias = dev_normal((n,), 0, 0.5, 63, F32)
+    c0 = dev_uniform((m, n), -1, 1, 64, dt_c)
+    desc_args = dict(m=m, n=n, k=k, trans_a=ta, trans_b=tb, alpha=0.5, beta=2.0, bias=bias, relu=True)
+    c_split, c_plain = c0.clone(), c0.clone()
+    d = cb.make_gemm_desc(a, b, c_split, **desc_args)
+    q = cb.gemm_query(d)
+    assert q.split_k > 1 and q.workspace_bytes >= q.workspace_min_bytes + q.split_k * m * n * 4
+    assert (q.workspace_min_bytes > 0) == (layout == "TN")  # K x M A with M = 300: rows not 16-byte aligned
+    assert q.tiles <= 148
+    ws = torch.empty(q.workspace_bytes, dtype=torch.uint8, device="cuda")
+    cb.gemm_desc(d, ws, q.workspace_bytes)
+    # the minimum workspace (repacks only) runs the unsplit plan
+    cb.gemm_desc(cb.make_gemm_desc(a, b, c_plain, **desc_args), ws, q.workspace_min_bytes)
+    cb.sync_status()
+    r = orc.gemm_f64(to_host(a), to_host(b), F16, trans_a=ta, trans_b=tb, alpha=0.5, beta=2.0,
+                     c0=to_host(c0), dtype_c0=dt_c, bias=to_host(bias), dtype_bias=F32, relu=True)
+    for c, what in ((c_split, "split"), (c_plain, "unsplit")):
+        got = to_host(c).astype(np.float64) if dt_c == F32 else as_f64(to_host(c), dt_c)
+        assert_close(got, r, what=f"{what} {layout} {dt_c}", k=k)
