@@ -312,25 +312,6 @@ int64_t tile_count(const TcConfig& c, int64_t m, int64_t n, int64_t items) {
   return ((m + rows - 1) / rows) * ((n + c.bn - 1) / c.bn) * items;
 }
 
-// Split K when the output has so few tiles that most SMs would idle through a
-// long reduction: the largest number of equal k-block ranges (at least 16
-// k-blocks = 1024 of K each) whose tiles still fit in one wave.
-void choose_split(const choreo_gemm_desc& d, GemmPlan& g, int sms) {
-  if (d.batch != 1) return;
-  const int64_t kb = (d.k + 63) / 64;
-  const int64_t slots = g.cfg.pair ? sms / 2 : sms;
-  if (kb < 32 || tile_count(g.cfg, d.m, d.n, 1) * 2 > slots) return;
-  for (int64_t s = 2; s <= 64 && kb / s >= 16; ++s) {
-    if (kb % s != 0) continue;
-    const TcConfig c = select_tile_config(d.m, d.n, kb / s, s, sms);
-    const int64_t slots_c = c.pair ? sms / 2 : sms;
-    if (tile_count(c, d.m, d.n, s) > slots_c) continue;
-    g.split = s;
-    g.split_cfg = c;
-  }
-  if (g.split > 1) g.split_bytes = round_up(g.split * d.m * d.n * 4, 256);
-}
-
 GemmPlan plan_tc(const choreo_gemm_desc& d) {
   GemmPlan g;
   g.a = plan_operand(d.a, d.lda, d.stride_a, d.batch, d.trans_a ? d.k : d.m, d.trans_a ? d.m : d.k);
@@ -339,8 +320,16 @@ GemmPlan plan_tc(const choreo_gemm_desc& d) {
   g.b.offset = g.a.bytes;
   g.workspace = g.a.bytes + g.b.bytes;
   const int sms = current_sm_count();
-  g.cfg = select_tc_config(d.m, d.n, d.k, d.batch, sms);
-  choose_split(d, g, sms);
+  const int64_t kb = (d.k + 63) / 64;
+  // The fastest plan, possibly with K split; and the unsplit fallback for a
+  // caller whose workspace holds no partials.
+  const TilePlan best = plan_tiles(d.m, d.n, kb, d.batch, sms, d.batch == 1, dtype_bytes(d.dtype_c));
+  g.cfg = best.split > 1 ? plan_tiles(d.m, d.n, kb, d.batch, sms, false, dtype_bytes(d.dtype_c)).cfg : best.cfg;
+  if (best.split > 1) {
+    g.split = best.split;
+    g.split_cfg = best.cfg;
+    g.split_bytes = round_up(g.split * d.m * d.n * 4, 256);
+  }
   return g;
 }
 

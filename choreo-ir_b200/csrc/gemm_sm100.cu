@@ -188,50 +188,12 @@ TcConfig select_tc_config(int64_t m, int64_t n, int64_t k, int64_t batch, int sm
   return select_tile_config(m, n, (k + kBK - 1) / kBK, batch, sm_count);
 }
 
-TcConfig select_tile_config(int64_t m, int64_t n, int64_t k_blocks, int64_t batch, int sm_count) {
-  // Candidates: wide CTA pairs (512 x 256 tiles on 2 SMs), CTA pairs
-  // (256 x BN) and single CTAs (128 x BN). Times are in units of one k-block
-  // of MMAs over a 128 x 256 slab on one SM; a tile puts rows_per_sm x BN
-  // outputs on each SM, i.e. `area` = rows_per_sm * BN / (128 * 256) slabs.
-  // Per tile the mainloop takes (k_blocks + fixed) * area / eff (`eff`: the
-  // candidate's relative tensor-pipe efficiency — shared-memory operand
-  // bandwidth per MMA and L2 traffic per FLOP favour wide tiles and pairs;
-  // `fixed`: pipeline fill) and the epilogue epi * area (the measured time to
-  // drain, convert and store one slab). Accumulators are released to the MMA
-  // issuer as soon as they are read, so the two overlap and a tile costs the
-  // larger of them; the whole launch costs waves * that.
-  struct Cand { const char* name; bool pair, wide; int bn; double eff, fixed, epi; };
-  const Cand cands[6] = {{"wide256", true, true, 256, 1.10, 6.0, 13.8},
-                         {"pair256", true, false, 256, 1.0, 4.0, 12.8},
-                         {"single256", false, false, 256, 0.97, 4.0, 9.3},
-                         {"pair128", true, false, 128, 0.92, 4.0, 19.7},
-                         {"single128", false, false, 128, 0.85, 4.0, 11.6},
-                         {"single64", false, false, 64, 0.6, 4.0, 16.0}};
-  const char* force = std::getenv("CHOREO_GEMM_TILE");  // e.g. "wide256", "single128" (tuning aid)
-  double best = 1e300;
+namespace {
+TcConfig make_config(bool pair, bool wide, int bn) {
   TcConfig c{};
-  for (const Cand& cd : cands) {
-    if (force && std::strcmp(force, cd.name) != 0) continue;
-    const int64_t rows = cd.wide ? 4 * kBM : (cd.pair ? 2 * kBM : kBM);
-    const int64_t rows_per_sm = cd.wide ? 2 * kBM : kBM;
-    const int64_t slots = cd.pair ? sm_count / 2 : sm_count;
-    const int64_t tiles = ((m + rows - 1) / rows) * ((n + cd.bn - 1) / cd.bn) * batch;
-    const int64_t waves = (tiles + slots - 1) / slots;
-    const double area = static_cast<double>(rows_per_sm * cd.bn) / (kBM * 256.0);
-    const double mainloop = (static_cast<double>(k_blocks) + cd.fixed) / cd.eff;
-    const double t = static_cast<double>(waves) * area * (mainloop > cd.epi ? mainloop : cd.epi);
-    if (t < best * 0.97) {
-      best = t;
-      c.pair = cd.pair;
-      c.wide = cd.wide;
-      c.bn = cd.bn;
-    }
-  }
-  if (best == 1e300) {  // unknown forced name: default choice
-    c.pair = true;
-    c.wide = false;
-    c.bn = 256;
-  }
+  c.pair = pair;
+  c.wide = wide;
+  c.bn = bn;
   if (c.wide) {
     c.stages = kWideStages;
     c.smem = tc_wide_smem_bytes<kWideStages>();
@@ -247,6 +209,77 @@ TcConfig select_tile_config(int64_t m, int64_t n, int64_t k_blocks, int64_t batc
   }
   c.group_m = 0;
   return c;
+}
+}  // namespace
+
+TilePlan plan_tiles(int64_t m, int64_t n, int64_t k_blocks, int64_t batch, int sm_count, bool allow_split,
+                    int out_bytes) {
+  // Candidates: wide CTA pairs (512 x 256 tiles on 2 SMs), CTA pairs
+  // (256 x BN) and single CTAs (128 x BN). A tile puts rows_per_sm x BN
+  // outputs on each SM, `area` = rows_per_sm * BN / (128 * 256) slabs. One
+  // k-block of a 128 x 256 slab takes kSlabUs / eff on one SM, where eff is
+  // the candidate's efficiency measured on B200 at full load (fp16
+  // 8192 x 8192 x 4096: operand bytes per FLOP from L2 decide it — the small
+  // tiles re-read A and B far more); `fixed` is the per-tile pipeline fill
+  // in k-blocks and `epi` the measured time to drain, convert and store one
+  // slab, in k-blocks. Accumulators go back to the MMA issuer as soon as
+  // they are read, so mainloop and epilogue overlap: a tile costs the larger
+  // of the two and the launch costs waves * that.
+  //
+  // With allow_split (one batch item), K may also be cut into `split` equal
+  // ranges of whole k-blocks (at least 8 each) run as the batch items of one
+  // launch, the partials (fp32) then summed by a second pass that costs its
+  // bytes at about 5 TB/s plus a launch. The cheapest (tile, split) wins.
+  struct Cand { const char* name; bool pair, wide; int bn; double eff, fixed, epi; };
+  const Cand cands[6] = {{"wide256", true, true, 256, 1.06, 6.0, 13.8},
+                         {"pair256", true, false, 256, 1.0, 3.0, 12.8},
+                         {"single256", false, false, 256, 0.93, 3.0, 9.3},
+                         {"pair128", true, false, 128, 0.63, 3.0, 19.7},
+                         {"single128", false, false, 128, 0.70, 3.0, 11.6},
+                         {"single64", false, false, 64, 0.36, 3.0, 16.0}};
+  constexpr double kSlabUs = 0.435;          // one k-block of a 128 x 256 slab, pair256, full load
+  constexpr double kReduceBytesPerUs = 5.0e6;
+  constexpr double kReduceLaunchUs = 3.0;
+  const char* force = std::getenv("CHOREO_GEMM_TILE");  // e.g. "wide256", "single128" (tuning aid)
+  const char* force_split = std::getenv("CHOREO_SPLIT_K");  // e.g. "1" (no split), "8" (tuning aid)
+  const int64_t want_split = force_split ? std::atoll(force_split) : 0;
+  TilePlan best{};
+  best.est_us = 1e300;
+  for (const Cand& cd : cands) {
+    if (force && std::strcmp(force, cd.name) != 0) continue;
+    const int64_t rows = cd.wide ? 4 * kBM : (cd.pair ? 2 * kBM : kBM);
+    const int64_t rows_per_sm = cd.wide ? 2 * kBM : kBM;
+    const int64_t slots = cd.pair ? sm_count / 2 : sm_count;
+    const int64_t tiles1 = ((m + rows - 1) / rows) * ((n + cd.bn - 1) / cd.bn) * batch;
+    const double area = static_cast<double>(rows_per_sm * cd.bn) / (kBM * 256.0);
+    for (int64_t split = 1; split <= 64; ++split) {
+      if (split > 1 && (!allow_split || batch != 1 || k_blocks % split != 0 || k_blocks / split < 8)) continue;
+      if (want_split > 0 && split != want_split) continue;
+      const int64_t tiles = tiles1 * split;
+      const int64_t waves = (tiles + slots - 1) / slots;
+      const double kb = static_cast<double>(k_blocks / split);
+      const double mainloop = (kb + cd.fixed) / cd.eff;
+      const double epi = split > 1 ? cd.epi * 4.0 / out_bytes : cd.epi;  // fp32 partials
+      double t = static_cast<double>(waves) * area * (mainloop > epi ? mainloop : epi) * kSlabUs;
+      if (split > 1)
+        t += static_cast<double>(m) * static_cast<double>(n) * (4.0 * split + out_bytes) / kReduceBytesPerUs +
+             kReduceLaunchUs;
+      if (t < best.est_us * 0.97) {
+        best.est_us = t;
+        best.cfg = make_config(cd.pair, cd.wide, cd.bn);
+        best.split = split;
+      }
+    }
+  }
+  if (best.est_us == 1e300) {  // unknown forced name or split: default choice
+    best.cfg = make_config(true, false, 256);
+    best.split = 1;
+  }
+  return best;
+}
+
+TcConfig select_tile_config(int64_t m, int64_t n, int64_t k_blocks, int64_t batch, int sm_count) {
+  return plan_tiles(m, n, k_blocks, batch, sm_count, false, 2).cfg;
 }
 
 int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream) {

@@ -67,6 +67,15 @@ TcConfig select_tc_config(int64_t m, int64_t n, int64_t k, int64_t batch, int sm
 inline int tile_rows_of(const TcConfig& c) { return c.wide ? 512 : (c.pair ? 256 : 128); }
 // Same choice from the K-block count (the convolution's K is R*S*ceil(C/64) blocks).
 TcConfig select_tile_config(int64_t m, int64_t n, int64_t k_blocks, int64_t batch, int sm_count);
+// The tile shape and, with allow_split (batch 1), the number of K splits with
+// the lowest estimated time; out_bytes is the size of one output element.
+struct TilePlan {
+  TcConfig cfg{};
+  int64_t split = 1;
+  double est_us = 0;
+};
+TilePlan plan_tiles(int64_t m, int64_t n, int64_t k_blocks, int64_t batch, int sm_count, bool allow_split,
+                    int out_bytes);
 
 // A GEMM with every operand already TMA-legal (16-byte aligned base, ld and
 // batch stride), in the orientation it is stored.
