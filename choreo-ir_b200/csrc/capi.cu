@@ -321,10 +321,45 @@ GemmPlan plan_tc(const choreo_gemm_desc& d) {
   g.workspace = g.a.bytes + g.b.bytes;
   const int sms = current_sm_count();
   const int64_t kb = (d.k + 63) / 64;
-  // The fastest plan, possibly with K split; and the unsplit fallback for a
-  // caller whose workspace holds no partials.
-  const TilePlan best = plan_tiles(d.m, d.n, kb, d.batch, sms, d.batch == 1, dtype_bytes(d.dtype_c));
-  g.cfg = best.split > 1 ? plan_tiles(d.m, d.n, kb, d.batch, sms, false, dtype_bytes(d.dtype_c)).cfg : best.cfg;
+  // The fastest plan, possibly with K split, and the unsplit fallback for a
+  // caller whose workspace holds no partials; the last shapes planned on
+  // this host thread are remembered (the cost model depends on nothing else).
+  struct Entry {
+    int64_t m, n, kb, batch;
+    int out_bytes, sms;
+    char tile_env[16];   // the tuning overrides the plan was made under
+    char split_env[16];
+    TilePlan best;
+    TcConfig unsplit;
+  };
+  thread_local Entry cache[32];
+  thread_local int cache_used = 0, cache_next = 0;
+  const int out_bytes = dtype_bytes(d.dtype_c);
+  char tile_env[16] = {0}, split_env[16] = {0};
+  if (const char* v = std::getenv("CHOREO_GEMM_TILE")) std::snprintf(tile_env, sizeof(tile_env), "%s", v);
+  if (const char* v = std::getenv("CHOREO_SPLIT_K")) std::snprintf(split_env, sizeof(split_env), "%s", v);
+  const Entry* hit = nullptr;
+  for (int i = 0; i < cache_used; ++i) {
+    const Entry& e = cache[i];
+    if (e.m == d.m && e.n == d.n && e.kb == kb && e.batch == d.batch && e.out_bytes == out_bytes && e.sms == sms &&
+        std::strcmp(e.tile_env, tile_env) == 0 && std::strcmp(e.split_env, split_env) == 0) {
+      hit = &e;
+      break;
+    }
+  }
+  if (hit == nullptr) {
+    Entry e{d.m, d.n, kb, d.batch, out_bytes, sms, {0}, {0}, {}, {}};
+    std::memcpy(e.tile_env, tile_env, sizeof(tile_env));
+    std::memcpy(e.split_env, split_env, sizeof(split_env));
+    e.best = plan_tiles(d.m, d.n, kb, d.batch, sms, d.batch == 1, out_bytes);
+    e.unsplit = e.best.split > 1 ? plan_tiles(d.m, d.n, kb, d.batch, sms, false, out_bytes).cfg : e.best.cfg;
+    cache[cache_next] = e;
+    hit = &cache[cache_next];
+    cache_next = (cache_next + 1) % 32;
+    if (cache_used < 32) ++cache_used;
+  }
+  const TilePlan best = hit->best;
+  g.cfg = hit->unsplit;
   if (best.split > 1) {
     g.split = best.split;
     g.split_cfg = best.cfg;

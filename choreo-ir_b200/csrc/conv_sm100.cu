@@ -113,8 +113,9 @@ int launch_conv_wide(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
                      int grid, cudaStream_t stream) {
   constexpr int smem = tc_wide_smem_bytes<kConvWideStages>();
   auto kern = tc_gemm_pair_wide_kernel<kConvWideStages, ConvLoader<128, true>, OutT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(conv wide)");
+  static std::atomic<uint64_t> attr_done{0};
+  if (int rc = set_smem_limit_once(kern, smem, attr_done, "cudaFuncSetAttribute(conv wide)")) return rc;
+  cudaError_t e;
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 wide CTA-pair conv launch");
@@ -127,8 +128,9 @@ int launch_conv_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensor
   constexpr int STAGES = conv_stages(BN);
   constexpr int smem = tc_smem_bytes<BN, STAGES>();
   auto kern = tc_gemm_kernel<BN, STAGES, ConvLoader<BN, false>, OutT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(conv)");
+  static std::atomic<uint64_t> attr_done{0};
+  if (int rc = set_smem_limit_once(kern, smem, attr_done, "cudaFuncSetAttribute(conv)")) return rc;
+  cudaError_t e;
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 conv launch");
@@ -141,8 +143,9 @@ int launch_conv_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
   constexpr int STAGES = conv_pair_stages(BN);
   constexpr int smem = tc_pair_smem_bytes<BN, STAGES>();
   auto kern = tc_gemm_pair_kernel<BN, STAGES, ConvLoader<BN / 2, true>, OutT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(conv pair)");
+  static std::atomic<uint64_t> attr_done{0};
+  if (int rc = set_smem_limit_once(kern, smem, attr_done, "cudaFuncSetAttribute(conv pair)")) return rc;
+  cudaError_t e;
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 CTA-pair conv launch");

@@ -107,8 +107,9 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& 
   constexpr int STAGES = stages_for(BN);
   constexpr int smem = tc_smem_bytes<BN, STAGES>();
   auto kern = tc_gemm_kernel<BN, STAGES, GemmLoader<A_MN, B_MN, BN, false>, OutT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
+  static std::atomic<uint64_t> attr_done{0};
+  if (int rc = set_smem_limit_once(kern, smem, attr_done, "cudaFuncSetAttribute(gemm)")) return rc;
+  cudaError_t e;
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch");
@@ -121,8 +122,9 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   constexpr int STAGES = pair_stages_for(BN);
   constexpr int smem = tc_pair_smem_bytes<BN, STAGES>();
   auto kern = tc_gemm_pair_kernel<BN, STAGES, GemmLoader<A_MN, B_MN, BN / 2, true>, OutT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm pair)");
+  static std::atomic<uint64_t> attr_done{0};
+  if (int rc = set_smem_limit_once(kern, smem, attr_done, "cudaFuncSetAttribute(gemm pair)")) return rc;
+  cudaError_t e;
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 CTA-pair GEMM launch");
@@ -134,8 +136,9 @@ int launch_wide(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
                 int grid, cudaStream_t stream) {
   constexpr int smem = tc_wide_smem_bytes<kWideStages>();
   auto kern = tc_gemm_pair_wide_kernel<kWideStages, GemmLoader<A_MN, B_MN, 128, true>, OutT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm wide)");
+  static std::atomic<uint64_t> attr_done{0};
+  if (int rc = set_smem_limit_once(kern, smem, attr_done, "cudaFuncSetAttribute(gemm wide)")) return rc;
+  cudaError_t e;
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 wide CTA-pair GEMM launch");

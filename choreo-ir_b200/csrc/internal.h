@@ -3,6 +3,7 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cstdint>
 #include <cstddef>
 
@@ -16,6 +17,21 @@ int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int ok();
 // Converts a CUDA runtime error into CHOREO_ERR_CUDA with context.
 int cuda_fail(cudaError_t e, const char* what);
+
+// Raises a kernel's dynamic shared-memory limit once per device: `done` is
+// the caller's per-kernel record (bit d set once device d has it).
+template <typename Kernel>
+int set_smem_limit_once(Kernel kern, int smem, std::atomic<uint64_t>& done, const char* what) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  const uint64_t bit = dev < 64 ? (uint64_t{1} << dev) : 0;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return CHOREO_OK;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  done.fetch_or(bit, std::memory_order_release);
+  return CHOREO_OK;
+}
 
 // Device status word of the current device (kernel-side failure record).
 uint32_t* status_word();
