@@ -717,14 +717,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------------------
 // Wide CTA-pair variant: the pair computes a 512 x 256 tile as two M = 256
-// halves that share every B k-block (two cta_group::2 MMAs per k-step). Each
-// CTA stages 2 x 128 A rows and 128 B columns per k-block and keeps a
-// 256 x 256 fp32 accumulator (its 128 rows of each half) in all 512 TMEM
-// columns: a quarter less L2 -> SM operand traffic per FLOP than 256 x 256
-// tiles. With no room for a second accumulator, overlap comes from draining
-// the accumulator in halves: the epilogue releases half 0 as soon as it has
-// read it, and the next tile's first pipeline-depth k-blocks issue their
-// half-0 MMAs while the epilogue is still reading half 1.
+// halves that share every B k-block (two cta_group::2 MMAs per k-step). CTA r
+// owns tile rows [256 r, 256 r + 256), staged per k-block as one 256-row A
+// box, plus 128 B columns; half h of the tile is rows [128 h, 128 h + 128) of
+// each CTA. Each CTA keeps its 256 x 256 fp32 accumulator (128 rows of each
+// half) in all 512 TMEM columns: a quarter less L2 -> SM operand traffic per
+// FLOP than 256 x 256 tiles. With no room for a second accumulator, overlap
+// comes from handing the accumulator back in halves: the epilogue releases
+// half 0 as soon as it has read it into registers, and the next tile's first
+// pipeline-depth k-blocks issue their half-0 MMAs while half 1 is being read.
 template <int STAGES>
 struct alignas(8) TcWideBarriers {
   uint64_t full[STAGES];
