@@ -382,17 +382,31 @@ int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream)
 
 // ------------------------------------------------------------------ repack
 namespace {
+// dst rows are ld_dst (a multiple of 8) elements, 16-byte aligned: each
+// thread writes 8 elements with one 16-byte store; the source rows may sit at
+// any 2-byte alignment, so they are read element by element (coalesced across
+// the warp, served from L1).
 __global__ void repack16_kernel(const uint16_t* __restrict__ src, int64_t ld_src, int64_t stride_src,
                                 uint16_t* __restrict__ dst, int64_t ld_dst, int64_t stride_dst,
                                 int64_t rows, int64_t cols) {
   const int64_t b = blockIdx.z;
   const uint16_t* s = src + b * stride_src;
   uint16_t* d = dst + b * stride_dst;
-  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
-    for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < ld_dst;
-         c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-      d[r * ld_dst + c] = c < cols ? s[r * ld_src + c] : uint16_t(0);
+  const int64_t chunks = ld_dst / 8;
+  const int64_t total = rows * chunks;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / chunks;
+    const int64_t c0 = (i - r * chunks) * 8;
+    const uint16_t* srow = s + r * ld_src;
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t lo = c0 + 2 * e < cols ? srow[c0 + 2 * e] : 0u;
+      const uint32_t hi = c0 + 2 * e + 1 < cols ? srow[c0 + 2 * e + 1] : 0u;
+      w[e] = lo | (hi << 16);
     }
+    *reinterpret_cast<uint4*>(d + r * ld_dst + c0) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 }  // namespace
@@ -401,9 +415,13 @@ int launch_repack16(const void* src, int64_t ld_src, int64_t stride_src, void* d
                     int64_t stride_dst, int64_t rows, int64_t cols, int64_t batch,
                     cudaStream_t stream) {
   if (batch > 65535) return fail(CHOREO_ERR_UNSUPPORTED, "repack: batch %lld > 65535", (long long)batch);
+  if (ld_dst % 8 != 0) return fail(CHOREO_ERR_INVALID_ARG, "repack: destination ld %lld not a multiple of 8",
+                                   (long long)ld_dst);
   dim3 block(256);
-  dim3 grid(static_cast<unsigned>(std::min<int64_t>((ld_dst + 255) / 256, 64)),
-            static_cast<unsigned>(std::min<int64_t>(rows, 65535)), static_cast<unsigned>(batch));
+  const int64_t work = rows * (ld_dst / 8);
+  dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256,
+                                                                         int64_t{8} * current_sm_count()))),
+            1, static_cast<unsigned>(batch));
   repack16_kernel<<<grid, block, 0, stream>>>(static_cast<const uint16_t*>(src), ld_src, stride_src,
                                               static_cast<uint16_t*>(dst), ld_dst, stride_dst, rows,
                                               cols);

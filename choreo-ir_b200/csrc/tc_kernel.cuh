@@ -52,7 +52,7 @@ struct TcParams {
   void* c;
   int64_t ldc, stride_c;   // elements
   int32_t c_vec_ok;        // 16-byte vector stores are legal for C
-  int32_t c_tma;           // C is TMA-addressable: the wide kernel stores through a staging tile
+  int32_t c_tma;           // C is TMA-addressable: the epilogues store through staging tiles
   float alpha, beta;
   const void* bias;
   int32_t dtype_bias;      // 8 f16, 9 f32, 11 bf16
@@ -501,7 +501,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     if (lane == 0) mbar_arrive(smem_u32(&bars->tmem_empty[buf]));
                                   });
     }
-    if (lane == 0) bulk_wait_all();  // staged stores finished before the CTA's shared memory goes away
+    // The staged stores have read their shared-memory source before the CTA's
+    // shared memory goes away; their global writes drain on their own.
+    if (lane == 0) bulk_wait_read_all();
     __syncwarp();
   }
 
@@ -703,7 +705,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                     }
                                   });
     }
-    if (lane == 0) bulk_wait_all();  // staged stores finished before the CTA's shared memory goes away
+    // The staged stores have read their shared-memory source before the CTA's
+    // shared memory goes away; their global writes drain on their own.
+    if (lane == 0) bulk_wait_read_all();
     __syncwarp();
   }
 
@@ -950,7 +954,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                     });
       }
     }
-    if (lane == 0) bulk_wait_all();  // staged stores finished before the CTA's shared memory goes away
+    // The staged stores have read their shared-memory source before the CTA's
+    // shared memory goes away; their global writes drain on their own.
+    if (lane == 0) bulk_wait_read_all();
     __syncwarp();
   }
 
