@@ -338,7 +338,7 @@ def bench_reference(args, spec: dict, world: int, rank: int) -> None:
                          "kind": "reference" if s["use_ref"] else "port", "sample": sample_text(s, spec)},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 class Case:
@@ -622,10 +622,29 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
     }
     if unit == "TFLOP/s":
         line["pct_of_nominal_dense_peak"] = 100.0 * value / (NOMINAL_DENSE_TFLOPS * world)
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_JSON_FD = None
+
+
+def emit(line: dict) -> None:
+    """The one JSON line, on the process's original standard output."""
+    data = (json.dumps(line) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, data)
 
 
 def main() -> None:
+    # Library banners (NCCL's version line, warnings) go to stderr: standard
+    # output carries the JSON line only.
+    global _JSON_FD
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
