@@ -39,6 +39,8 @@ def run_conv(cb, x, w, dt_out, stride=1, pad=1, dil=1, bias=None, relu=False, al
     (1, 15, 15, 64, 32, 3, 3, 1, 2, 2),      # dilation 2
     (1, 9, 9, 64, 64, 3, 3, 1, 0, 1),        # no padding
     (4, 7, 5, 16, 8, 3, 3, 1, 1, 1),         # tiny
+    (1, 10, 10, 16, 3, 3, 3, 2, 0, 1),       # 3 output channels: rows not 16-byte aligned, scalar stores
+    (2, 13, 9, 8, 72, 3, 3, 1, 1, 1),        # C = 8, the smallest channel count
 ])
 @pytest.mark.parametrize("dt", [F16, BF16])
 def test_conv_small_full(cb, cuda, orc, n, h, w, c, k, r, s, stride, pad, dil, dt):
