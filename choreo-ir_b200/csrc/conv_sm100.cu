@@ -116,8 +116,7 @@ int launch_conv_wide(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
   static std::atomic<uint64_t> attr_done{0};
   if (int rc = set_smem_limit_once(kern, smem, attr_done, "cudaFuncSetAttribute(conv wide)")) return rc;
   cudaError_t e;
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, ta, tb, tc, kp);
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 wide CTA-pair conv launch");
   return CHOREO_OK;
 }
@@ -131,8 +130,7 @@ int launch_conv_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensor
   static std::atomic<uint64_t> attr_done{0};
   if (int rc = set_smem_limit_once(kern, smem, attr_done, "cudaFuncSetAttribute(conv)")) return rc;
   cudaError_t e;
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, ta, tb, tc, kp);
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 conv launch");
   return CHOREO_OK;
 }
@@ -146,8 +144,7 @@ int launch_conv_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
   static std::atomic<uint64_t> attr_done{0};
   if (int rc = set_smem_limit_once(kern, smem, attr_done, "cudaFuncSetAttribute(conv pair)")) return rc;
   cudaError_t e;
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, ta, tb, tc, kp);
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 CTA-pair conv launch");
   return CHOREO_OK;
 }

@@ -110,8 +110,7 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& 
   static std::atomic<uint64_t> attr_done{0};
   if (int rc = set_smem_limit_once(kern, smem, attr_done, "cudaFuncSetAttribute(gemm)")) return rc;
   cudaError_t e;
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, ta, tb, tc, kp);
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch");
   return CHOREO_OK;
 }
@@ -125,8 +124,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   static std::atomic<uint64_t> attr_done{0};
   if (int rc = set_smem_limit_once(kern, smem, attr_done, "cudaFuncSetAttribute(gemm pair)")) return rc;
   cudaError_t e;
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, ta, tb, tc, kp);
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 CTA-pair GEMM launch");
   return CHOREO_OK;
 }
@@ -139,8 +137,7 @@ int launch_wide(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   static std::atomic<uint64_t> attr_done{0};
   if (int rc = set_smem_limit_once(kern, smem, attr_done, "cudaFuncSetAttribute(gemm wide)")) return rc;
   cudaError_t e;
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, tc, kp);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, ta, tb, tc, kp);
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 wide CTA-pair GEMM launch");
   return CHOREO_OK;
 }
@@ -391,6 +388,7 @@ namespace {
 __global__ void repack16_kernel(const uint16_t* __restrict__ src, int64_t ld_src, int64_t stride_src,
                                 uint16_t* __restrict__ dst, int64_t ld_dst, int64_t stride_dst,
                                 int64_t rows, int64_t cols) {
+  griddep_launch_dependents();  // the GEMM that reads the repack may start its prologue
   const int64_t b = blockIdx.z;
   const uint16_t* s = src + b * stride_src;
   uint16_t* d = dst + b * stride_dst;

@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <atomic>
+#include <utility>
 #include <cstdint>
 #include <cstddef>
 
@@ -31,6 +32,25 @@ int set_smem_limit_once(Kernel kern, int smem, std::atomic<uint64_t>& done, cons
   if (e != cudaSuccess) return cuda_fail(e, what);
   done.fetch_or(bit, std::memory_order_release);
   return CHOREO_OK;
+}
+
+// Launches `kern` with programmatic stream serialization: the grid may start
+// while the previous kernel in the stream is finishing; the kernel's
+// griddep_wait() orders its global accesses after that kernel.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // Device status word of the current device (kernel-side failure record).

@@ -29,6 +29,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
                                                             int64_t n, OutT* __restrict__ c, int64_t ldc, float alpha,
                                                             float beta, const void* __restrict__ bias, int dtype_bias,
                                                             int relu) {
+  choreo_sm100::griddep_wait();  // the first pass's partials are complete and visible
   const int64_t quads = (n + 3) / 4;
   const int64_t total = m * quads;
   const bool vec = (n % 4) == 0;
@@ -70,9 +71,9 @@ int launch_typed(const float* part, int64_t split, int64_t m, int64_t n, void* c
                  const void* bias, int dtype_bias, int relu, cudaStream_t stream) {
   const int64_t total = m * ((n + 3) / 4);
   const int64_t blocks = std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(current_sm_count()) * 16);
-  splitk_reduce_kernel<OutT><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-      part, split, m, n, static_cast<OutT*>(c), ldc, alpha, beta, bias, dtype_bias, relu);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = launch_pdl(splitk_reduce_kernel<OutT>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                                   stream, part, split, m, n, static_cast<OutT*>(c), ldc, alpha, beta, bias,
+                                   dtype_bias, relu);
   return e == cudaSuccess ? CHOREO_OK : cuda_fail(e, "split-K reduction launch");
 }
 

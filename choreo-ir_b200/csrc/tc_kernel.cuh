@@ -404,6 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      griddep_wait();  // the previous kernel's writes to A and B are visible
       const uint64_t pol_a = l2_policy(p.l2_policy_a);
       const uint64_t pol_b = l2_policy(p.l2_policy_b);
       uint32_t stage = 0, phase = 0, issued = 0;
@@ -424,6 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
+      griddep_launch_dependents();  // every load is issued: the next kernel may start launching
       if (!ok) {
         // Let the loads already in flight land before the CTA exits.
         const uint32_t inflight = issued < STAGES ? issued : STAGES;
@@ -480,6 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;       // TMEM lanes this warp may read
     const int col_half = (warp - 2) >> 2;  // which half of the columns
     const uint32_t stage_buf = smem_u32(s_stage) + static_cast<uint32_t>(warp - 2) * 4096u;
+    griddep_wait();  // the previous kernel is done with C
     uint32_t local = 0;
     for (int64_t t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
       const uint32_t buf = local & 1;
@@ -590,6 +593,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producers (both CTAs)
     if (lane == 0) {
+      griddep_wait();  // the previous kernel's writes to A and B are visible
       const uint64_t pol_a = l2_policy(p.l2_policy_a);
       const uint64_t pol_b = l2_policy(p.l2_policy_b);
       uint32_t stage = 0, phase = 0, issued = 0;
@@ -612,6 +616,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
+      griddep_launch_dependents();  // every load is issued: the next kernel may start launching
       if (!ok) {
         if (leader) {
           const uint32_t inflight = issued < STAGES ? issued : STAGES;
@@ -677,6 +682,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int col_half = (warp - 2) >> 2;
     const uint32_t stage_buf = smem_u32(s_stage) + static_cast<uint32_t>(warp - 2) * 4096u;
+    griddep_wait();  // the previous kernel is done with C
     uint32_t local = 0;
     for (int64_t t = cluster_id; t < p.num_tiles; t += num_clusters, ++local) {
       const uint32_t buf = local & 1;
@@ -803,6 +809,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producers (both CTAs)
     if (lane == 0) {
+      griddep_wait();  // the previous kernel's writes to A and B are visible
       const uint64_t pol_a = l2_policy(p.l2_policy_a);
       const uint64_t pol_b = l2_policy(p.l2_policy_b);
       uint32_t stage = 0, phase = 0, issued = 0;
@@ -827,6 +834,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
+      griddep_launch_dependents();  // every load is issued: the next kernel may start launching
       if (!ok) {
         if (leader) {
           const uint32_t inflight = issued < STAGES ? issued : STAGES;
@@ -925,6 +933,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int col_half = (warp - 2) >> 2;
     const uint32_t stage_buf = smem_u32(s_stage) + static_cast<uint32_t>(warp - 2) * 4096u;
+    griddep_wait();  // the previous kernel is done with C
     uint32_t local = 0;
     for (int64_t t = cluster_id; t < p.num_tiles; t += num_clusters, ++local) {
       int ready = 0;
