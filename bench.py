@@ -430,15 +430,9 @@ def setup_conv(cb, spec, world, rank, dev, stream) -> Case:
     case.step = lambda: cb.conv2d_desc(d, stream=stream)
     x_h, w_h, b_h = _pinned_copy(x), _pinned_copy(wt), _pinned_copy(bias)
     o_h = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-
-    def e2e():
-        x.copy_(x_h, non_blocking=True)
-        wt.copy_(w_h, non_blocking=True)
-        bias.copy_(b_h, non_blocking=True)
-        case.step()
-        o_h.copy_(out, non_blocking=True)
-
-    case.e2e_step = e2e
+    plan = cb.HostConvPlan(imgs, spec["h"], spec["w"], spec["c"], spec["k"], spec["r"], spec["s"], torch.float16,
+                           stride=spec["stride"], padding=spec["pad"], bias=True, relu=spec["relu"], device=dev)
+    case.e2e_step = lambda: plan.run(x_h, w_h, o_h, b_h, stream=stream)
     case.h2d = sum(t.numel() * t.element_size() for t in (x_h, w_h, b_h))
     case.d2h = o_h.numel() * o_h.element_size()
     case.flops, case.bytes_ = spec_flops_bytes({**spec, "n": imgs})
@@ -452,7 +446,9 @@ def setup_conv(cb, spec, world, rank, dev, stream) -> Case:
                  f"batch split over {world} GPUs ({imgs} images on rank {rank}), weights replicated, "
                  "no collective",
                  "tile": f"{q.tile_m}x{q.tile_n}x{q.tile_k}", "cluster": q.cluster_m, "stages": q.stages,
-                 "grid": q.grid_x}
+                 "grid": q.grid_x,
+                 "e2e": f"HostConvPlan: pinned host activations/weights/bias in, output out; {plan.launches()} "
+                        "runs of images, copies in, convolutions and copies out on three streams"}
     return case
 
 

@@ -268,6 +268,63 @@ class HostGemmPlan:
         return len(self.slabs)
 
 
+class HostConvPlan:
+    """conv2d for NHWC activations and KRSC weights in pinned HOST memory,
+    pipelined over the PCIe links like HostGemmPlan: the batch is cut into
+    runs of images; the weights, the bias and every run of activations go to
+    the device on one copy stream, each run's convolution starts on the
+    caller's stream as soon as its images have landed, and each run of output
+    goes back to the host on a second copy stream."""
+
+    def __init__(self, n, h, w, c, k, r, s, dtype, *, stride=1, padding=1, dilation=1, bias=False, relu=False,
+                 runs=None, device=None):
+        import torch
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        p = (h + 2 * padding - dilation * (r - 1) - 1) // stride + 1
+        q = (w + 2 * padding - dilation * (s - 1) - 1) // stride + 1
+        self.x = torch.empty(n, h, w, c, device=self.device, dtype=dtype)
+        self.wt = torch.empty(k, r, s, c, device=self.device, dtype=dtype)
+        self.out = torch.empty(n, p, q, k, device=self.device, dtype=dtype)
+        self.bias = torch.empty(k, device=self.device, dtype=dtype) if bias else None
+        if runs is None:
+            runs = max(1, min(8, n // 2))
+        per = -(-n // max(1, runs))
+        self.runs = [(i0, min(per, n - i0)) for i0 in range(0, n, per)]
+        self.descs = [conv_desc(self.x[i0:i0 + cnt], self.wt, self.out[i0:i0 + cnt], stride=stride, padding=padding,
+                                dilation=dilation, bias=self.bias, relu=relu) for i0, cnt in self.runs]
+        for d in self.descs:
+            if conv2d_query(d).workspace_bytes:
+                raise ValueError("HostConvPlan: the convolution needs a workspace")
+        self.s_in = torch.cuda.Stream(self.device)
+        self.s_out = torch.cuda.Stream(self.device)
+        self.ev_in = [torch.cuda.Event() for _ in self.runs]
+        self.ev_conv = [torch.cuda.Event() for _ in self.runs]
+
+    def run(self, x_h, w_h, out_h, bias_h=None, stream=None):
+        import torch
+        st = torch.cuda.current_stream(self.device) if stream is None else stream
+        self.s_in.wait_stream(st)
+        self.s_out.wait_stream(st)
+        with torch.cuda.stream(self.s_in):
+            self.wt.copy_(w_h, non_blocking=True)
+            if self.bias is not None:
+                self.bias.copy_(bias_h, non_blocking=True)
+            for (i0, cnt), ev in zip(self.runs, self.ev_in):
+                self.x[i0:i0 + cnt].copy_(x_h[i0:i0 + cnt], non_blocking=True)
+                ev.record(self.s_in)
+        for (i0, cnt), d, ev_in, ev_c in zip(self.runs, self.descs, self.ev_in, self.ev_conv):
+            st.wait_event(ev_in)
+            conv2d_desc(d, stream=st)
+            ev_c.record(st)
+            self.s_out.wait_event(ev_c)
+            with torch.cuda.stream(self.s_out):
+                out_h[i0:i0 + cnt].copy_(self.out[i0:i0 + cnt], non_blocking=True)
+        st.wait_stream(self.s_out)
+
+    def launches(self) -> int:
+        return len(self.runs)
+
+
 def conv_desc(x, w, out, *, stride=1, padding=1, dilation=1, bias=None, relu=False, alpha=1.0) -> ConvDesc:
     """x: NHWC, w: KRSC, out: NHWC (torch tensors, contiguous)."""
     d = ConvDesc()

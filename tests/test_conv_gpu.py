@@ -111,3 +111,24 @@ def test_conv_forced_tiles(cb, cuda, orc, monkeypatch, tile):
     assert q.cluster_m == (2 if tile.startswith(("pair", "wide")) else 1)
     ref = orc.conv2d_f64(x, wt, F16, bias=bias, dtype_bias=F32, relu=True)
     assert_close(as_f64(to_host(out), F16).reshape(-1, 192), ref, what=f"conv {tile}", k=9 * 128)
+
+
+def test_host_conv_plan_pipelined(cb, cuda, orc):
+    """HostConvPlan: pinned host activations, weights and bias in, output out,
+    image runs overlapped on three streams (a shorter last run included),
+    against fp64 on sampled pixels."""
+    import torch
+    n, h, w, c, k = 5, 12, 10, 64, 96
+    plan = cb.HostConvPlan(n, h, w, c, k, 3, 3, torch.float16, bias=True, relu=True, runs=2)
+    assert [cnt for _, cnt in plan.runs] == [3, 2]
+    x = orc.to_bits(orc.uniform((n, h, w, c), 0, 1, 71), F16)
+    wt = orc.to_bits(orc.normal((k, 3, 3, c), 0, 1.0 / 24, 72), F16)
+    bias = orc.to_bits(orc.normal((k,), 0, 0.1, 73), F16)
+    as_t = lambda a: torch.from_numpy(a.view(np.int16)).view(torch.float16).pin_memory()
+    out = torch.zeros(n, h, w, k, dtype=torch.float16).pin_memory()
+    plan.run(as_t(x), as_t(wt), out, as_t(bias))
+    torch.cuda.current_stream().synchronize()
+    cb.sync_status()
+    ref = orc.conv2d_f64(x, wt, F16, bias=bias, dtype_bias=F16, relu=True)
+    got = as_f64(out.view(torch.int16).numpy().view(np.uint16), F16).reshape(-1, k)
+    assert_close(got, ref, what="host conv plan", k=9 * c)
