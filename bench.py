@@ -10,7 +10,9 @@ distributions; nothing is read from disk):
   sharded   row-sharded bf16 GEMM M=65536, N=K=8192, U[-0.5,0.5], bias ~N(0,0.1)
             fused with ReLU, bf16 output; rows split across the N ranks
             (strong scaling: total work fixed), B and bias replicated, no
-            collective on the data path. The default at N > 1.
+            collective on the data path. The default at N > 1; there the
+            replication of B from rank 0 and the gather of the C slabs onto
+            rank 0 are timed apart over NCCL (config.exchanges_outside_timing).
   custom    GEMM of --shape MxNxK and --dtype (U[-1,1], NN).
   smallk    fp16 GEMM 16384 x 16384 x 128: output-write (HBM) bound.
   conv      implicit-GEMM conv2d NHWC fp16, N=32, 56x56, C=K=256, 3x3, s1 p1,
@@ -386,6 +388,7 @@ def setup_gemm(cb, spec, world, rank, dev, stream) -> Case:
     case.h2d = sum(t.numel() * t.element_size() for t in (a_h, b_h, bias_h) if t is not None)
     case.d2h = c_h.numel() * c_h.element_size()
     case.rows = rows
+    case.b_dev, case.c_dev = b, c
     case.flops, case.bytes_ = spec_flops_bytes(spec, rows)
     case.units_total = spec_flops_bytes(spec)[0]
     case.flush = case.bytes_ - 2.0 * rows * N <= L2_BYTES      # A + B (+ bias) fit in L2
@@ -477,6 +480,47 @@ def setup_relu(cb, spec, world, rank, dev, stream) -> Case:
     return case
 
 
+def time_exchanges(case, world: int, rank: int, dev, stream) -> dict:
+    """The two exchanges around a row-sharded GEMM, timed apart from it over
+    NCCL (NVLink / NVSwitch): replicating B from rank 0 to every rank, and
+    gathering the C slabs onto rank 0. Every rank runs both, in this order;
+    times are the max over ranks of CUDA-event time on the launching stream."""
+    import torch
+    import torch.distributed as dist
+    b, c = case.b_dev, case.c_dev
+    rows = torch.tensor([c.shape[0]], device=dev, dtype=torch.int64)
+    all_rows = [torch.zeros_like(rows) for _ in range(world)]
+    dist.all_gather(all_rows, rows)
+    equal = len({int(r.item()) for r in all_rows}) == 1
+    gather_list = [torch.empty_like(c) for _ in range(world)] if (rank == 0 and equal) else None
+
+    def timed(fn, reps=3):
+        fn()  # warm-up (communicator set-up)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0])
+
+    out = {}
+    ms_b = timed(lambda: dist.broadcast(b, src=0))
+    nbytes_b = b.numel() * b.element_size()
+    out["b_broadcast"] = {"ms": ms_b, "bytes": nbytes_b, "GB/s": nbytes_b / (ms_b * 1e-3) / 1e9,
+                          "how": "NCCL broadcast from rank 0"}
+    if equal:
+        ms_c = timed(lambda: dist.gather(c, gather_list=gather_list, dst=0))
+        nbytes_c = c.numel() * c.element_size() * (world - 1)
+        out["c_gather"] = {"ms": ms_c, "bytes_into_rank0": nbytes_c, "GB/s": nbytes_c / (ms_c * 1e-3) / 1e9,
+                           "how": "NCCL gather of the C slabs onto rank 0"}
+    return out
+
+
 def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> None:
     import torch
     import torch.distributed as dist
@@ -560,6 +604,9 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
         sampler.mark(t_wall2, t_wall3)
         clocks = sampler.stop()
 
+    # ---------------------------------------------------------- the sharded GEMM's exchanges, timed apart
+    exchange = time_exchanges(case, world, rank, dev, stream) if world > 1 and spec["kind"] == "gemm" else None
+
     # ---------------------------------------------------------- max over ranks
     t = torch.tensor([ms, ms_e2e], device=dev, dtype=torch.float64)
     if world > 1:
@@ -592,6 +639,8 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
         cpu = {"value": s["units"] / secs / scale, "unit": unit, "cores": s["threads"],
                "kind": "reference" if s["use_ref"] else "port", "sample": sample_text(s, spec),
                "seconds": round(secs, 2)}
+    if exchange is not None:
+        case.info["exchanges_outside_timing"] = exchange
     config = {"workload": spec["workload"], **case.info,
               "l2": ("L2 flushed (256 MB written) between timed launches; per-launch events" if case.flush
                      else "inputs larger than the 126 MB L2 (no flush needed)")}
