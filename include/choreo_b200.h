@@ -198,9 +198,10 @@ int choreo_gemm_noalloc(const choreo_gemm_desc* d, void* stream);
  * device devices[i]'s slab (its own A rows, its replica of B and bias, its C
  * rows). One host thread per device launches on streams[i] (NULL = default
  * stream) and, if ms_out != NULL, synchronizes and stores that device's
- * kernel time in ms_out[i]. No data crosses between devices. Stands behind
- * the multi-GPU split of north-star item (5); the reference has no
- * multi-GPU code (core/device.hpp:136-156 only switches devices). */
+ * kernel time in ms_out[i]. No data crosses between devices. The M-row
+ * split of a large GEMM across the GPUs of one box, B replicated; the
+ * reference has no multi-GPU code (core/device.hpp:136-156 only switches
+ * devices). */
 int choreo_gemm_rowsharded(const choreo_gemm_desc* descs, int ngpu, const int* devices,
                            void* const* streams, float* ms_out);
 

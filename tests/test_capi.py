@@ -161,7 +161,7 @@ def test_shard_rows_partition(cb, m, n):
             assert r0 % 128 == 0 and (rows % 128 == 0 or r0 + rows == m)
 
 
-def test_shard_rows_config4(cb):
+def test_shard_rows_65536_rows(cb):
     assert [cb.shard_rows(65536, 8, r) for r in range(8)] == [(8192 * r, 8192) for r in range(8)]
 
 

@@ -60,7 +60,7 @@ def test_conv_f32_output_and_alpha(cb, cuda, orc):
     assert_close(to_host(out).reshape(-1, 64).astype(np.float64), ref, what="conv f32 out")
 
 
-def test_config5_resnet_layer(cb, cuda, orc):
+def test_conv_32x56x56x256_3x3_layer(cb, cuda, orc):
     """N=32, 56x56, C=K=256, 3x3, stride 1, pad 1, fp16; activations U[0,1],
     weights N(0, std = 1/sqrt(2304)), bias N(0, 0.1); fused bias + ReLU.
     Checked on 400 sampled output pixels (image borders included) against
@@ -79,7 +79,7 @@ def test_config5_resnet_layer(cb, cuda, orc):
     xh, wh, bh = to_host(x), to_host(wt), to_host(bias)
     ref = orc.conv2d_f64(xh, wh, F16, bias=bh, dtype_bias=F16, relu=True, pixels=pix)
     got = as_f64(to_host(out.reshape(-1, K)[torch.from_numpy(pix).cuda()]), F16)
-    assert_close(got, ref, what="config5", k=9 * Cc)
+    assert_close(got, ref, what="32x56x56x256 3x3", k=9 * Cc)
     # the reference conv loop (fp16 accumulation) on the first 8 pixels of image 0
     ref16 = as_f64(orc.ref_conv2d_f16(xh[:1], wh, 1, 1, pix=(0, 8)), F16)
     pre = orc.conv2d_f64(xh[:1], wh, F16, pixels=np.arange(8))

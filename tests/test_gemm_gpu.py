@@ -83,22 +83,22 @@ def test_golden_reference_outputs(cb, cuda, orc, name):
         assert orc.normwise_err(as_f64(c, dt), r64) <= orc.normwise_err(ref, r64)
 
 
-# ------------------------------------------------------------------ config 1: 1024x1024x512 fp16 U[-1,1]
-def test_config1_against_fp64_and_reference_path(cb, cuda, orc):
+# ------------------------------------------------------------------ 1024x1024x512 fp16 U[-1,1]
+def test_gemm_1024x1024x512_against_fp64_and_reference_path(cb, cuda, orc):
     M, N, K = 1024, 1024, 512
     a = orc.to_bits(orc.uniform((M, K), -1, 1, 42), F16)
     b = orc.to_bits(orc.uniform((K, N), -1, 1, 43), F16)
     c = as_f64(to_host(run(cb, to_dev(a, F16), to_dev(b, F16), M, N, K, F16, F16)), F16)
     r64 = orc.gemm_f64(a, b, F16)
-    assert_close(c, r64, what="config1")
+    assert_close(c, r64, what="1024x1024x512")
     ref = as_f64(orc.ref_matmul(a, b, F16, nthreads=orc.threads()), F16)
     assert orc.normwise_err(c, ref) <= TOL
     assert orc.normwise_err(c, r64) < orc.normwise_err(ref, r64)
 
 
-# ------------------------------------------------------------------ config 2: square sweep
+# ------------------------------------------------------------------ square sweep 2048 / 4096 / 8192
 @pytest.mark.parametrize("dt", [F16, BF16])
-def test_config2_2048_full(cb, cuda, orc, dt):
+def test_square_2048_full(cb, cuda, orc, dt):
     n = 2048
     a = orc.to_bits(orc.uniform((n, n), -1, 1, 1), dt)
     b = orc.to_bits(orc.uniform((n, n), -1, 1, 2), dt)
@@ -108,7 +108,7 @@ def test_config2_2048_full(cb, cuda, orc, dt):
 
 @pytest.mark.parametrize("dt", [F16, BF16])
 @pytest.mark.parametrize("n", [4096, 8192])
-def test_config2_large_sampled_and_checksums(cb, cuda, orc, dt, n):
+def test_square_large_sampled_and_checksums(cb, cuda, orc, dt, n):
     import torch
     a = dev_uniform((n, n), -1, 1, 10 + n, dt)
     b = dev_uniform((n, n), -1, 1, 20 + n, dt)
@@ -130,7 +130,7 @@ def test_config2_large_sampled_and_checksums(cb, cuda, orc, dt, n):
     assert torch.allclose(c64.sum(1), row, rtol=0, atol=2e-3 * float(row.abs().max()) + 1e-6 * n)
 
 
-def test_config2_deterministic(cb, cuda):
+def test_square_deterministic(cb, cuda):
     import torch
     a = dev_uniform((2048, 2048), -1, 1, 5, F16)
     b = dev_uniform((2048, 2048), -1, 1, 6, F16)
@@ -139,9 +139,9 @@ def test_config2_deterministic(cb, cuda):
     assert torch.equal(c1, c2)
 
 
-# ------------------------------------------------------------------ config 3: ragged NN/NT/TN
+# ------------------------------------------------------------------ ragged 4097x3000x1536 NN/NT/TN
 @pytest.mark.parametrize("layout", ["NN", "NT", "TN", "TT"])
-def test_config3_ragged_layouts(cb, cuda, orc, layout):
+def test_ragged_4097x3000x1536_layouts(cb, cuda, orc, layout):
     import torch
     M, N, K = 4097, 3000, 1536
     ta, tb = layout[0] == "T", layout[1] == "T"
@@ -150,15 +150,15 @@ def test_config3_ragged_layouts(cb, cuda, orc, layout):
     c = run(cb, a, b, M, N, K, F16, F16, trans_a=ta, trans_b=tb)
     rows = sample_rows(M, 64, seed=3)
     r = orc.gemm_f64(to_host(a), to_host(b), F16, trans_a=ta, trans_b=tb, rows=rows)
-    assert_close(as_f64(to_host(c[torch.from_numpy(rows).cuda()]), F16), r, what=f"config3 {layout}", k=K)
+    assert_close(as_f64(to_host(c[torch.from_numpy(rows).cuda()]), F16), r, what=f"4097x3000x1536 {layout}", k=K)
     A = a.double().t() if ta else a.double()
     B = b.double().t() if tb else b.double()
     col = A.sum(0) @ B
     assert torch.allclose(c.double().sum(0), col, rtol=0, atol=2e-3 * float(col.abs().max()) + 1e-2)
 
 
-# ------------------------------------------------------------------ config 4: row-sharded 65536x8192x8192 bf16
-def test_config4_full_and_slabs(cb, cuda, orc):
+# ------------------------------------------------------------------ row-sharded 65536x8192x8192 bf16
+def test_rowsharded_65536x8192x8192_full_and_slabs(cb, cuda, orc):
     import torch
     M, N, K = 65536, 8192, 8192
     a = dev_uniform((M, K), -0.5, 0.5, 41, BF16)
@@ -168,7 +168,7 @@ def test_config4_full_and_slabs(cb, cuda, orc):
     rows = sample_rows(M, 40, seed=4, tile=8192)
     r = orc.gemm_f64(to_host(a[torch.from_numpy(rows).cuda()]), to_host(b), BF16, bias=to_host(bias),
                      dtype_bias=BF16, relu=True)
-    assert_close(as_f64(to_host(c[torch.from_numpy(rows).cuda()]), BF16), r, what="config4 rows", k=K)
+    assert_close(as_f64(to_host(c[torch.from_numpy(rows).cuda()]), BF16), r, what="65536x8192x8192 rows", k=K)
     # Each rank's slab computed on its own equals the same rows of the full GEMM.
     for rank in (0, 3, 7):
         r0, nrows = cb.shard_rows(M, 8, rank)
@@ -177,7 +177,7 @@ def test_config4_full_and_slabs(cb, cuda, orc):
     del c
 
 
-# ------------------------------------------------------------------ config 5 lives in test_conv_gpu.py
+# ------------------------------------------------------------------ the 32x56x56x256 3x3 conv lives in test_conv_gpu.py
 
 # ------------------------------------------------------------------ edge cases
 @pytest.mark.parametrize("m,n,k", [(1, 1, 1), (1, 300, 70), (300, 1, 70), (129, 257, 65), (7, 9, 17),
