@@ -231,10 +231,20 @@ def test_padded_leading_dims_use_workspace(cb, cuda, orc):
     a, b = a_full[:, :k], b_full[:, :n]
     d = cb.make_gemm_desc(a, b, torch.empty(m, n, device="cuda", dtype=torch.float16), m=m, n=n, k=k,
                           lda=a.stride(0), ldb=b.stride(0))
-    assert cb.gemm_query(d).workspace_bytes > 0
+    q = cb.gemm_query(d)
+    assert q.workspace_bytes > 0 and q.workspace_min_bytes > 0
     with pytest.raises(cb.ChoreoError) as e:
         cb.gemm_desc(d)
     assert e.value.code == cb.ERR_WORKSPACE
+    ws = torch.empty(q.workspace_bytes + 512, dtype=torch.uint8, device="cuda")
+    with pytest.raises(cb.ChoreoError) as e:  # one byte short of the repacks
+        cb.gemm_desc(d, ws, q.workspace_min_bytes - 1)
+    assert e.value.code == cb.ERR_WORKSPACE
+    with pytest.raises(cb.ChoreoError) as e:  # not 256-byte aligned
+        cb.gemm_desc(d, ws.data_ptr() + 16, q.workspace_bytes)
+    assert e.value.code == cb.ERR_WORKSPACE and "256-byte" in str(e.value)
+    cb.gemm_desc(d, ws, q.workspace_min_bytes)  # exactly the repacks
+    cb.sync_status()
     c = run(cb, a, b, m, n, k, F16, F16)
     r = orc.gemm_f64(to_host(a), to_host(b), F16)
     assert_close(as_f64(to_host(c), F16), r, what="padded")
