@@ -733,14 +733,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // each CTA. Each CTA keeps its 256 x 256 fp32 accumulator (128 rows of each
 // half) in all 512 TMEM columns: a quarter less L2 -> SM operand traffic per
 // FLOP than 256 x 256 tiles. With no room for a second accumulator, overlap
-// comes from handing the accumulator back in halves: the epilogue releases
-// half 0 as soon as it has read it into registers, and the next tile's first
-// pipeline-depth k-blocks issue their half-0 MMAs while half 1 is being read.
+// comes from handing the accumulator over in halves at both ends of a tile:
+// the last pipeline-depth k-blocks issue their half-0 MMAs first and publish
+// half 0, so the epilogue reads it out while the same stages are replayed for
+// half 1; the epilogue releases each half as soon as it has read it into
+// registers, and the next tile's first pipeline-depth k-blocks issue their
+// half-0 MMAs while half 1 is being read.
 template <int STAGES>
 struct alignas(8) TcWideBarriers {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
-  uint64_t tmem_full;      // this tile's accumulator is complete (leader commit, count 1)
+  uint64_t tmem_full[2];   // accumulator half h of this tile is complete (leader commit, count 1)
   uint64_t tmem_empty[2];  // accumulator half h read out by the pair's 16 epilogue warps (leader's, count 16)
   uint64_t drain;
   uint32_t tmem_base;
@@ -787,7 +790,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&bars->empty[s]), 1);
     }
     if (p.c_tma) tma_prefetch_desc(&tma_c);
-    mbar_init(smem_u32(&bars->tmem_full), 1);
+    mbar_init(smem_u32(&bars->tmem_full[0]), 1);
+    mbar_init(smem_u32(&bars->tmem_full[1]), 1);
     mbar_init(smem_u32(&bars->tmem_empty[0]), 2 * kEpiWarps);
     mbar_init(smem_u32(&bars->tmem_empty[1]), 2 * kEpiWarps);
     mbar_init(smem_u32(&bars->drain), 1);
@@ -898,6 +902,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (++st == STAGES) { st = 0; ph ^= 1; }
         }
         if (!ok) break;
+        auto publish = [&](int h) {  // half h of the tile is complete once its MMAs finish
+          const uint32_t fb = smem_u32(&bars->tmem_full[h]);
+          umma_commit_pair(fb);
+          umma_commit_pair(mapa_shared(fb, 1));
+        };
+        if (D == p.num_k_blocks) publish(0);
         if (!mbar_wait(smem_u32(&bars->tmem_empty[1]), tph ^ 1, wctx, kStatusTimeoutMma)) {
           ok = false;
           break;
@@ -908,8 +918,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           release(stage);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
-        // Steady state: both halves per stage.
-        for (int kb = D; kb < p.num_k_blocks; ++kb) {
+        // Steady state: both halves per stage, up to the tail.
+        const int T = (p.num_k_blocks - D) < STAGES ? (p.num_k_blocks - D) : STAGES;
+        for (int kb = D; kb < p.num_k_blocks - T; ++kb) {
           if (!mbar_wait(smem_u32(&bars->full[stage]), phase, wctx, kStatusTimeoutMma)) {
             ok = false;
             break;
@@ -921,9 +932,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        const uint32_t fb = smem_u32(&bars->tmem_full);
-        umma_commit_pair(fb);
-        umma_commit_pair(mapa_shared(fb, 1));
+        // Tail: the last T stages are consumed for half 0, which is then
+        // published so the epilogue drains it while the same stages are
+        // replayed for half 1 — the half-0 drain overlaps T k-blocks of MMAs.
+        if (T > 0) {
+          st = stage;
+          ph = phase;
+          for (int kb = p.num_k_blocks - T; kb < p.num_k_blocks; ++kb) {
+            if (!mbar_wait(smem_u32(&bars->full[st]), ph, wctx, kStatusTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_half(0, st, kb);
+            if (++st == STAGES) { st = 0; ph ^= 1; }
+          }
+          if (!ok) break;
+          publish(0);
+          for (int kb = p.num_k_blocks - T; kb < p.num_k_blocks; ++kb) {
+            issue_half(1, stage, kb);
+            release(stage);
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          }
+        }
+        publish(1);
       }
       umma_commit_pair(smem_u32(&bars->drain));
       mbar_wait(smem_u32(&bars->drain), 0, wctx, kStatusTimeoutDrain, false);
@@ -935,17 +967,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t stage_buf = smem_u32(s_stage) + static_cast<uint32_t>(warp - 2) * 4096u;
     griddep_wait();  // the previous kernel is done with C
     uint32_t local = 0;
-    for (int64_t t = cluster_id; t < p.num_tiles; t += num_clusters, ++local) {
-      int ready = 0;
-      if (lane == 0)
-        ready = mbar_wait(smem_u32(&bars->tmem_full), local & 1, wctx, kStatusTimeoutEpilogue) ? 1 : 0;
-      ready = __shfl_sync(0xffffffffu, ready, 0);
-      if (!ready) break;
-      tc_fence_after();
+    bool ok = true;
+    for (int64_t t = cluster_id; t < p.num_tiles && ok; t += num_clusters, ++local) {
       int b, mb, nb;
       tile_coords(t, p, b, mb, nb);
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
+        int ready = 0;
+        if (lane == 0)
+          ready = mbar_wait(smem_u32(&bars->tmem_full[h]), local & 1, wctx, kStatusTimeoutEpilogue) ? 1 : 0;
+        ready = __shfl_sync(0xffffffffu, ready, 0);
+        if (!ready) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         const uint32_t taddr =
             tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + h * BN + col_half * (BN / 2);
         epilogue_warp<BN / 2, OutT>(taddr, nb * BN + col_half * (BN / 2),
