@@ -352,6 +352,7 @@ class Case:
     units_total = 0.0  # whole-job FLOPs (or bytes) per step
     flops = bytes_ = 0.0  # this rank's algorithmic FLOPs / bytes per launch
     flush = False      # inputs + outputs fit in L2: flush between timed launches
+    launches_per_step = 1
     info: dict = {}
 
 
@@ -377,9 +378,13 @@ def setup_gemm(cb, spec, world, rank, dev, stream) -> Case:
     c = torch.empty(rows, N, device=dev, dtype=dt)
     desc = cb.make_gemm_desc(a, b, c, m=rows, n=N, k=K, bias=bias, relu=spec["relu"])
     q = cb.gemm_query(desc)
-    assert q.workspace_bytes == 0
     case = Case()
-    case.step = lambda: cb.gemm_desc(desc, stream=stream)
+    # Row-major operands with 16-byte rows never need a repack; a workspace is
+    # only the fp32 partials of a K split (few output tiles over a long K).
+    assert q.workspace_min_bytes == 0
+    ws = torch.empty(max(1, q.workspace_bytes), dtype=torch.uint8, device=dev)
+    case.step = lambda: cb.gemm_desc(desc, ws, q.workspace_bytes, stream=stream)
+    case.launches_per_step = 2 if q.split_k > 1 else 1  # the split's reduction pass
     a_h, b_h = _pinned_copy(a), _pinned_copy(b)
     bias_h = _pinned_copy(bias) if bias is not None else None
     c_h = torch.empty(rows, N, dtype=dt, pin_memory=True)
@@ -395,6 +400,7 @@ def setup_gemm(cb, spec, world, rank, dev, stream) -> Case:
     case.info = {
         "m": M_total, "n": N, "k": K, "layout": spec["layout"],
         "inputs": f"{spec['dist']} seeded on device; fp32 accumulation; {spec['dtype']} output",
+        "split_k": int(q.split_k),
         "epilogue": "bias+ReLU" if spec["bias"] else "none",
         "parallelism": f"row-sharded over {world} GPU(s), B replicated, no collective" if world > 1 else "single GPU",
         "rows_per_rank": rows, "tile": f"{q.tile_m}x{q.tile_n}x{q.tile_k}", "cluster": q.cluster_m,
@@ -661,7 +667,7 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
         "roofline": roof,
         "e2e": {"value": e2e_value, "unit": unit, "h2d_bytes_per_step": case.h2d, "d2h_bytes_per_step": case.d2h,
                 "steps": e2e_steps, "ms_per_step": ms_e2e_max / e2e_steps},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * case.launches_per_step,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
