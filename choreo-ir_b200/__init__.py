@@ -235,9 +235,12 @@ class HostGemmPlan:
         self.slabs = [(r0, min(per, m - r0)) for r0 in range(0, m, per)]
         self.descs = [make_gemm_desc(self.a[r0:r0 + rows], self.b, self.c[r0:r0 + rows], m=rows, n=n, k=k,
                                      bias=self.bias, relu=relu) for r0, rows in self.slabs]
-        for d in self.descs:
-            if gemm_query(d).workspace_min_bytes:
-                raise ValueError("HostGemmPlan: operands must be TMA-legal (16-byte aligned rows)")
+        qs = [gemm_query(d) for d in self.descs]
+        if any(q.workspace_min_bytes for q in qs):
+            raise ValueError("HostGemmPlan: operands must be TMA-legal (16-byte aligned rows)")
+        # One workspace (K-split partials) serves every slab: the slabs' GEMMs run in order on one stream.
+        self.ws_bytes = max(q.workspace_bytes for q in qs)
+        self.ws = torch.empty(max(1, self.ws_bytes), dtype=torch.uint8, device=self.device)
         self.s_in = torch.cuda.Stream(self.device)
         self.s_out = torch.cuda.Stream(self.device)
         self.ev_in = [torch.cuda.Event() for _ in self.slabs]
@@ -257,7 +260,7 @@ class HostGemmPlan:
                 ev.record(self.s_in)
         for (r0, rows), d, ev_in, ev_g in zip(self.slabs, self.descs, self.ev_in, self.ev_gemm):
             s.wait_event(ev_in)
-            gemm_desc(d, stream=s)
+            gemm_desc(d, self.ws, self.ws_bytes, stream=s)
             ev_g.record(s)
             self.s_out.wait_event(ev_g)
             with torch.cuda.stream(self.s_out):
