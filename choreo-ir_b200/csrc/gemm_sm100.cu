@@ -217,29 +217,31 @@ TilePlan plan_tiles(int64_t m, int64_t n, int64_t k_blocks, int64_t batch, int s
   // Candidates: wide CTA pairs (512 x 256 tiles on 2 SMs), CTA pairs
   // (256 x BN) and single CTAs (128 x BN). A tile puts rows_per_sm x BN
   // outputs on each SM, `area` = rows_per_sm * BN / (128 * 256) slabs. One
-  // k-block of a 128 x 256 slab takes kSlabUs / eff on one SM, where eff is
-  // the candidate's efficiency measured on B200 at full load (fp16
-  // 8192 x 8192 x 4096: operand bytes per FLOP from L2 decide it — the small
-  // tiles re-read A and B far more); `fixed` is the per-tile pipeline fill
-  // in k-blocks and `epi` the measured time to drain, convert and store one
-  // slab, in k-blocks (fp16 16384 x 16384 x 128). Checked against forced-tile
-  // timings of 8192 x 8192 x 512 and 16384 x 16384 x 128: within 10 % for the
-  // tile shapes the model picks. Accumulators go back to the MMA issuer as soon as
-  // they are read, so mainloop and epilogue overlap: a tile costs the larger
-  // of the two and the launch costs waves * that.
+  // k-block of a 128 x 256 slab takes kSlabUs / eff on one SM; `fixed` is the
+  // per-tile pipeline fill in k-blocks and `epi` the time to drain, convert
+  // and store one slab, in k-blocks. Accumulators go back to the MMA issuer as
+  // soon as they are read, so mainloop and epilogue overlap: a tile costs the
+  // larger of the two, the launch costs waves * that plus kLaunchUs. The
+  // constants are a least-squares fit (rms log error 0.08) to forced-tile
+  // timings on B200 of every candidate at ten shapes: 16384 x 16384 x {64,
+  // 128, 256}, 8192 x 8192 x {512, 2048}, 2048^3, 4096^3, 4097 x 3000 x 1536,
+  // 1024 x 1024 x 512, 3072 x 3072 x 1024 (operand bytes per FLOP from L2
+  // set eff; the pair tiles' epilogue is cheap since the peer CTA hands its
+  // accumulator back with a CTA-scope arrive).
   //
   // With allow_split (one batch item), K may also be cut into `split` equal
   // ranges of whole k-blocks (at least 8 each) run as the batch items of one
   // launch, the partials (fp32) then summed by a second pass that costs its
   // bytes at about 5 TB/s plus a launch. The cheapest (tile, split) wins.
   struct Cand { const char* name; bool pair, wide; int bn; double eff, fixed, epi; };
-  const Cand cands[6] = {{"wide256", true, true, 256, 1.06, 6.0, 7.1},
-                         {"pair256", true, false, 256, 1.0, 3.0, 7.9},
-                         {"single256", false, false, 256, 0.93, 3.0, 5.8},
-                         {"pair128", true, false, 128, 0.63, 3.0, 12.2},
-                         {"single128", false, false, 128, 0.70, 3.0, 7.2},
-                         {"single64", false, false, 64, 0.36, 3.0, 10.0}};
-  constexpr double kSlabUs = 0.435;          // one k-block of a 128 x 256 slab, pair256, full load
+  const Cand cands[6] = {{"wide256", true, true, 256, 1.21, 3.3, 4.1},
+                         {"pair256", true, false, 256, 1.01, 2.3, 4.4},
+                         {"single256", false, false, 256, 0.89, 2.5, 2.2},
+                         {"pair128", true, false, 128, 0.55, 1.3, 5.7},
+                         {"single128", false, false, 128, 0.61, 1.4, 5.6},
+                         {"single64", false, false, 64, 0.33, 0.9, 11.4}};
+  constexpr double kSlabUs = 0.435;          // one k-block of a 128 x 256 slab at eff 1
+  constexpr double kLaunchUs = 6.0;          // launch, ramp and the last tile's drain
   constexpr double kReduceBytesPerUs = 5.0e6;
   constexpr double kReduceLaunchUs = 3.0;
   const char* force = std::getenv("CHOREO_GEMM_TILE");  // e.g. "wide256", "single128" (tuning aid)
@@ -262,7 +264,7 @@ TilePlan plan_tiles(int64_t m, int64_t n, int64_t k_blocks, int64_t batch, int s
       const double kb = static_cast<double>(k_blocks / split);
       const double mainloop = (kb + cd.fixed) / cd.eff;
       const double epi = split > 1 ? cd.epi * 4.0 / out_bytes : cd.epi;  // fp32 partials
-      double t = static_cast<double>(waves) * area * (mainloop > epi ? mainloop : epi) * kSlabUs;
+      double t = kLaunchUs + static_cast<double>(waves) * area * (mainloop > epi ? mainloop : epi) * kSlabUs;
       if (split > 1)
         t += static_cast<double>(m) * static_cast<double>(n) * (4.0 * split + out_bytes) / kReduceBytesPerUs +
              kReduceLaunchUs;

@@ -208,9 +208,14 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// Arrive once on an mbarrier of another CTA of the cluster.
+// Arrive once on an mbarrier of another CTA of the cluster, with the
+// default (CTA-scope release) semantics. The callers hand back tensor memory:
+// their tcgen05.ld reads are complete (tcgen05.wait::ld) and ordered by
+// tcgen05.fence::before_thread_sync, so no cluster-scope release of generic
+// memory is needed — and one costs the arriving warp 1-2.5k cycles on B200,
+// which the MMA issuer waiting on the barrier then pays too.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // L2 eviction-priority policies for the cache_hint operand.
