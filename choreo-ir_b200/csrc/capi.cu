@@ -238,6 +238,7 @@ int validate_gemm(const choreo_gemm_desc* d) {
   if (d->m > INT32_MAX || d->n > INT32_MAX || d->k > INT32_MAX)
     return fail(CHOREO_ERR_UNSUPPORTED, "GEMM: dimensions above 2^31-1 are not supported");
   if (d->batch < 1) return fail(CHOREO_ERR_INVALID_ARG, "GEMM: batch must be >= 1");
+  if (d->batch > INT32_MAX) return fail(CHOREO_ERR_UNSUPPORTED, "GEMM: batch above 2^31-1 is not supported");
   if (d->a == nullptr) return fail(CHOREO_ERR_INVALID_ARG, "GEMM: Input tensor A has null data pointer");
   if (d->b == nullptr) return fail(CHOREO_ERR_INVALID_ARG, "GEMM: Input tensor B has null data pointer");
   if (d->c == nullptr) return fail(CHOREO_ERR_INVALID_ARG, "GEMM: Output tensor C has null data pointer");

@@ -105,6 +105,7 @@ def _desc(cb, **kw):
     (dict(ldc=3), -1, "ldc=3"),
     (dict(batch=0), -1, "batch"),
     (dict(m=1 << 31), -2, "2^31"),
+    (dict(batch=1 << 31), -2, "batch above 2^31-1"),
 ])
 def test_gemm_contract_errors(cb, kw, code, msg):
     d = _desc(cb, **kw)
