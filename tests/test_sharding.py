@@ -1,4 +1,4 @@
-"""Row-sharded multi-process logic on CPU: world-size-2 gloo ranks (127.0.0.1).
+"""Row-sharded multi-process logic on CPU: world-size-2 and -4 gloo ranks (127.0.0.1).
 
 Each rank takes its slab from choreo_shard_rows (the partition the GPU bench
 uses), computes its rows of C with the fp64 oracle, and rank 0 gathers the
@@ -81,11 +81,11 @@ def _worker(rank: int, world: int, port: int, mode: str, out_dir: str) -> None:
     dist.destroy_process_group()
 
 
-def _spawn(mode: str, tmp_path) -> list[int]:
+def _spawn(mode: str, tmp_path, world: int = 2) -> list[int]:
     import torch.multiprocessing as mp
     port = _free_port()
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, str(tmp_path))) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, str(tmp_path))) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -104,6 +104,15 @@ def _spawn(mode: str, tmp_path) -> list[int]:
 def test_row_sharded_slabs_assemble_to_full_result(tmp_path):
     codes = _spawn("ok", tmp_path)
     assert codes == [0, 0]
+    assert (tmp_path / "result").read_text() == "ok"
+
+
+def test_four_ranks_one_with_an_empty_shard(tmp_path):
+    """Four ranks over M = 300 rows (three 128-row tiles): the last rank owns
+    no rows, takes part in every collective all the same, and the slabs still
+    assemble to the full result."""
+    codes = _spawn("ok", tmp_path, world=4)
+    assert codes == [0, 0, 0, 0]
     assert (tmp_path / "result").read_text() == "ok"
 
 
