@@ -61,6 +61,13 @@ class ConvDesc(C.Structure):
     ]
 
 
+class Tuning(C.Structure):
+    _fields_ = [
+        ("tile", C.c_char * 16), ("split_k", C.c_int32), ("group_m", C.c_int32),
+        ("l2_policy_a", C.c_int32), ("l2_policy_b", C.c_int32), ("wait_timeout_ms", C.c_double),
+    ]
+
+
 class DeviceProps(C.Structure):
     _fields_ = [
         ("device", C.c_int32), ("cc_major", C.c_int32), ("cc_minor", C.c_int32),
@@ -76,6 +83,8 @@ _SIGNATURES = {
     "choreo_device_props_get": (C.c_int, [C.c_int, C.POINTER(DeviceProps)]),
     "choreo_sync_status": (C.c_int, [C.c_void_p]),
     "choreo_selftest_wait_timeout": (C.c_int, [C.c_double, C.c_void_p]),
+    "choreo_tuning_set": (C.c_int, [C.POINTER(Tuning)]),
+    "choreo_tuning_get": (C.c_int, [C.POINTER(Tuning)]),
     "choreo_gemm_query": (C.c_int, [C.POINTER(GemmDesc), C.POINTER(LaunchConfig)]),
     "choreo_gemm": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p, C.c_size_t, C.c_void_p]),
     "choreo_gemm_noalloc": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p]),
@@ -383,6 +392,42 @@ def sync_status(stream=None) -> None:
 
 def selftest_wait_timeout(timeout_ms: float, stream=None) -> None:
     check(lib.choreo_selftest_wait_timeout(timeout_ms, _stream_ptr(stream)))
+
+
+def get_tuning() -> Tuning:
+    t = Tuning()
+    check(lib.choreo_tuning_get(C.byref(t)))
+    return t
+
+
+def set_tuning(*, tile: str = "", split_k: int = 0, group_m: int = 0, l2_policy_a: int = -1,
+               l2_policy_b: int = -1, wait_timeout_ms: float = 0.0) -> None:
+    """Installs dispatcher overrides (choreo_tuning_set); the defaults leave
+    every choice to the library."""
+    t = Tuning()
+    t.tile = tile.encode()
+    t.split_k, t.group_m = split_k, group_m
+    t.l2_policy_a, t.l2_policy_b = l2_policy_a, l2_policy_b
+    t.wait_timeout_ms = wait_timeout_ms
+    check(lib.choreo_tuning_set(C.byref(t)))
+
+
+class tuning:
+    """Context manager: `with tuning(tile="pair256"): ...` applies the
+    overrides for the block and restores the previous settings after it."""
+
+    def __init__(self, **kw):
+        self.kw = kw
+        self.saved = None
+
+    def __enter__(self):
+        self.saved = get_tuning()
+        set_tuning(**self.kw)
+        return self
+
+    def __exit__(self, *exc):
+        check(lib.choreo_tuning_set(C.byref(self.saved)))
+        return False
 
 
 def shard_rows(m: int, nshards: int, rank: int) -> tuple[int, int]:

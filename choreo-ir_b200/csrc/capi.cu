@@ -103,6 +103,32 @@ uint32_t* status_word() {
   return c.status[dev];
 }
 
+namespace {
+// Process-wide tuning settings. Readers keep a per-thread copy and refresh it
+// only when the generation moves, so the common path takes no lock.
+std::mutex g_tuning_mu;
+choreo_tuning g_tuning = {{0}, 0, 0, -1, -1, 0.0};
+std::atomic<uint64_t> g_tuning_gen{1};
+
+bool known_tile(const char* s) {
+  static const char* const names[] = {"wide256", "pair256", "pair128", "single256", "single128", "single64"};
+  for (const char* n : names)
+    if (std::strcmp(s, n) == 0) return true;
+  return false;
+}
+}  // namespace
+
+Tuning tuning() {
+  thread_local Tuning cached{{{0}, 0, 0, -1, -1, 0.0}, 0};
+  const uint64_t gen = g_tuning_gen.load(std::memory_order_acquire);
+  if (cached.generation != gen) {
+    std::lock_guard<std::mutex> lk(g_tuning_mu);
+    cached.t = g_tuning;
+    cached.generation = g_tuning_gen.load(std::memory_order_relaxed);
+  }
+  return cached;
+}
+
 L2Plan l2_plan() {
   // Tiles walk N inside a group of M tiles covering 4096 rows: the group's A
   // panels are reused by every later tile of the group, so A is kept in L2
@@ -113,26 +139,16 @@ L2Plan l2_plan() {
   // 95.3 % with 2048, 93-94 % with 1024 or 8192 rows; the other eviction
   // hints were 0.5-1.5 % slower.
   L2Plan p{1, 0, 4096, 0};
-  if (const char* s = std::getenv("CHOREO_L2_POLICY")) {
-    if (s[0] >= '0' && s[0] <= '2' && s[1] >= '0' && s[1] <= '2') {
-      p.policy_a = s[0] - '0';
-      p.policy_b = s[1] - '0';
-    }
-  }
-  if (const char* s = std::getenv("CHOREO_GROUP_M")) {
-    const int g = std::atoi(s);
-    if (g >= 1 && g <= 1024) p.group_m = g;
-  }
+  const Tuning t = tuning();
+  if (t.t.l2_policy_a >= 0) p.policy_a = t.t.l2_policy_a;
+  if (t.t.l2_policy_b >= 0) p.policy_b = t.t.l2_policy_b;
+  if (t.t.group_m > 0) p.group_m = t.t.group_m;
   return p;
 }
 
 uint64_t wait_timeout_ns() {
-  static const uint64_t v = [] {
-    const char* s = std::getenv("CHOREO_WAIT_TIMEOUT_MS");
-    const double ms = s ? std::atof(s) : 2000.0;
-    return static_cast<uint64_t>((ms > 0 ? ms : 2000.0) * 1e6);
-  }();
-  return v;
+  const double ms = tuning().t.wait_timeout_ms;
+  return static_cast<uint64_t>((ms > 0 ? ms : 2000.0) * 1e6);
 }
 
 namespace {
@@ -328,30 +344,25 @@ GemmPlan plan_tc(const choreo_gemm_desc& d) {
   struct Entry {
     int64_t m, n, kb, batch;
     int out_bytes, sms;
-    char tile_env[16];   // the tuning overrides the plan was made under
-    char split_env[16];
+    uint64_t tuning_gen;   // the tuning settings the plan was made under
     TilePlan best;
     TcConfig unsplit;
   };
   thread_local Entry cache[32];
   thread_local int cache_used = 0, cache_next = 0;
   const int out_bytes = dtype_bytes(d.dtype_c);
-  char tile_env[16] = {0}, split_env[16] = {0};
-  if (const char* v = std::getenv("CHOREO_GEMM_TILE")) std::snprintf(tile_env, sizeof(tile_env), "%s", v);
-  if (const char* v = std::getenv("CHOREO_SPLIT_K")) std::snprintf(split_env, sizeof(split_env), "%s", v);
+  const uint64_t gen = tuning().generation;
   const Entry* hit = nullptr;
   for (int i = 0; i < cache_used; ++i) {
     const Entry& e = cache[i];
     if (e.m == d.m && e.n == d.n && e.kb == kb && e.batch == d.batch && e.out_bytes == out_bytes && e.sms == sms &&
-        std::strcmp(e.tile_env, tile_env) == 0 && std::strcmp(e.split_env, split_env) == 0) {
+        e.tuning_gen == gen) {
       hit = &e;
       break;
     }
   }
   if (hit == nullptr) {
-    Entry e{d.m, d.n, kb, d.batch, out_bytes, sms, {0}, {0}, {}, {}};
-    std::memcpy(e.tile_env, tile_env, sizeof(tile_env));
-    std::memcpy(e.split_env, split_env, sizeof(split_env));
+    Entry e{d.m, d.n, kb, d.batch, out_bytes, sms, gen, {}, {}};
     e.best = plan_tiles(d.m, d.n, kb, d.batch, sms, d.batch == 1, out_bytes);
     e.unsplit = e.best.split > 1 ? plan_tiles(d.m, d.n, kb, d.batch, sms, false, out_bytes).cfg : e.best.cfg;
     cache[cache_next] = e;
@@ -412,6 +423,35 @@ int choreo_sync_status(void* stream) {
     cudaMemcpy(w, &zero, sizeof(zero), cudaMemcpyHostToDevice);
     return fail(CHOREO_ERR_TIMEOUT, "a kernel pipeline wait expired (status 0x%x)", v);
   }
+  return ok();
+}
+
+int choreo_tuning_set(const choreo_tuning* t) {
+  choreo_tuning v = {{0}, 0, 0, -1, -1, 0.0};
+  if (t != nullptr) {
+    v = *t;
+    v.tile[sizeof(v.tile) - 1] = 0;
+    if (v.tile[0] != 0 && !known_tile(v.tile))
+      return fail(CHOREO_ERR_INVALID_ARG, "tuning: unknown tile \"%s\"", v.tile);
+    if (v.split_k < 0 || v.split_k > 64) return fail(CHOREO_ERR_INVALID_ARG, "tuning: split_k %d outside 0..64", v.split_k);
+    if (v.group_m < 0 || v.group_m > 1024)
+      return fail(CHOREO_ERR_INVALID_ARG, "tuning: group_m %d outside 0..1024", v.group_m);
+    if (v.l2_policy_a < -1 || v.l2_policy_a > 2 || v.l2_policy_b < -1 || v.l2_policy_b > 2)
+      return fail(CHOREO_ERR_INVALID_ARG, "tuning: L2 policy codes are -1, 0, 1 or 2");
+    if (!(v.wait_timeout_ms >= 0.0) || v.wait_timeout_ms > 3.6e6)
+      return fail(CHOREO_ERR_INVALID_ARG, "tuning: wait_timeout_ms outside 0..3.6e6");
+  }
+  {
+    std::lock_guard<std::mutex> lk(g_tuning_mu);
+    g_tuning = v;
+    g_tuning_gen.fetch_add(1, std::memory_order_release);
+  }
+  return ok();
+}
+
+int choreo_tuning_get(choreo_tuning* out) {
+  if (out == nullptr) return fail(CHOREO_ERR_INVALID_ARG, "tuning: null output");
+  *out = tuning().t;
   return ok();
 }
 
@@ -579,24 +619,34 @@ int choreo_gemm_rowsharded(const choreo_gemm_desc* descs, int ngpu, const int* d
         return;
       }
       cudaStream_t s = streams ? static_cast<cudaStream_t>(streams[i]) : nullptr;
+      if (ms_out == nullptr) {
+        rcs[i] = choreo_gemm(&descs[i], nullptr, 0, s);
+        msgs[i] = g_last_error;
+        return;
+      }
+      // Timed: ms_out[i] is the shard's device time, or -1 if none was measured.
+      ms_out[i] = -1.f;
       cudaEvent_t e0 = nullptr, e1 = nullptr;
-      if (ms_out) {
-        cudaEventCreate(&e0);
-        cudaEventCreate(&e1);
-        cudaEventRecord(e0, s);
-      }
-      rcs[i] = choreo_gemm(&descs[i], nullptr, 0, s);
-      if (ms_out) {
-        cudaEventRecord(e1, s);
+      if ((e = cudaEventCreate(&e0)) != cudaSuccess || (e = cudaEventCreate(&e1)) != cudaSuccess) {
+        rcs[i] = cuda_fail(e, "cudaEventCreate");
+      } else if ((e = cudaEventRecord(e0, s)) != cudaSuccess) {
+        rcs[i] = cuda_fail(e, "cudaEventRecord");
+      } else {
+        rcs[i] = choreo_gemm(&descs[i], nullptr, 0, s);
         if (rcs[i] == CHOREO_OK) {
-          cudaEventSynchronize(e1);
           float ms = 0.f;
-          cudaEventElapsedTime(&ms, e0, e1);
-          ms_out[i] = ms;
+          if ((e = cudaEventRecord(e1, s)) != cudaSuccess)
+            rcs[i] = cuda_fail(e, "cudaEventRecord");
+          else if ((e = cudaEventSynchronize(e1)) != cudaSuccess)
+            rcs[i] = cuda_fail(e, "cudaEventSynchronize");
+          else if ((e = cudaEventElapsedTime(&ms, e0, e1)) != cudaSuccess)
+            rcs[i] = cuda_fail(e, "cudaEventElapsedTime");
+          else
+            ms_out[i] = ms;
         }
-        cudaEventDestroy(e0);
-        cudaEventDestroy(e1);
       }
+      if (e0) cudaEventDestroy(e0);
+      if (e1) cudaEventDestroy(e1);
       msgs[i] = g_last_error;
     });
   }

@@ -244,9 +244,9 @@ TilePlan plan_tiles(int64_t m, int64_t n, int64_t k_blocks, int64_t batch, int s
   constexpr double kLaunchUs = 6.0;          // launch, ramp and the last tile's drain
   constexpr double kReduceBytesPerUs = 5.0e6;
   constexpr double kReduceLaunchUs = 3.0;
-  const char* force = std::getenv("CHOREO_GEMM_TILE");  // e.g. "wide256", "single128" (tuning aid)
-  const char* force_split = std::getenv("CHOREO_SPLIT_K");  // e.g. "1" (no split), "8" (tuning aid)
-  const int64_t want_split = force_split ? std::atoll(force_split) : 0;
+  const Tuning tu = tuning();  // forced tile name / split count (tests and tuning sweeps)
+  const char* force = tu.t.tile[0] != 0 ? tu.t.tile : nullptr;
+  const int64_t want_split = tu.t.split_k;
   TilePlan best{};
   best.est_us = 1e300;
   for (const Cand& cd : cands) {

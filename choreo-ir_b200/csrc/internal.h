@@ -68,10 +68,18 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                 CUtensorMapSwizzle swizzle);
 
+// The settings choreo_tuning_set installed (defaults unless a test or a
+// tuning sweep changed them), with a generation number that changes on
+// every set so cached plans can tell they are stale.
+struct Tuning {
+  choreo_tuning t;
+  uint64_t generation;
+};
+Tuning tuning();
+
 // L2 eviction policy codes handed to the kernels (A operand, B operand) and
-// the tile rasterisation group: defaults, overridable for tuning through
-// CHOREO_L2_POLICY="<a><b>" (digits: 0 normal, 1 evict_last, 2 evict_first)
-// and CHOREO_GROUP_M.
+// the tile rasterisation group: defaults, or the tuning overrides
+// (choreo_tuning::l2_policy_a/b, group_m).
 struct L2Plan {
   int policy_a, policy_b;
   int group_rows;   // rows of A walked together (group = group_rows / tile rows M tiles)

@@ -5,28 +5,36 @@
 // a plugin inside a host runtime that owns every device buffer and hands the
 // plugin's enqueue call only its inputs and outputs, or a latency-critical
 // loop that must not allocate (cudaMalloc can synchronize the device and
-// fragment a pre-planned memory budget). choreo_gemm needs a caller-provided
-// workspace when an operand is not 16-byte aligned (base, leading dimension
-// or batch stride) and has to be repacked before the TMA can read it; this
-// entry point stages that repack in a scratch array compiled into the
+// fragment a pre-planned memory budget). choreo_gemm uses a caller-provided
+// workspace for two things: repacking an operand that is not 16-byte aligned
+// (base, leading dimension or batch stride) before the TMA can read it, and
+// the fp32 partial sums of a K split (a GEMM with few output tiles over a
+// long K, cut into K ranges that run side by side and are summed by a second
+// pass). This entry point stages both in a scratch array compiled into the
 // library instead, so the caller passes inputs and outputs only.
 //
 // The scratch array is a file-scope __device__ array of
 // CHOREO_GEMM_NOALLOC_SCRATCH_BYTES. Every GPU that loads the library holds
-// it until the process exits. Requests whose repack needs more are rejected
-// with CHOREO_ERR_WORKSPACE before anything is launched.
+// it until the process exits. Requests whose repack alone needs more are
+// rejected with CHOREO_ERR_WORKSPACE before anything is launched; a K split
+// whose partials do not fit beside the repack runs unsplit instead.
 //
-// Set-up: the first call on a device (with that device current) resolves
-// the array's device address with cudaGetSymbolAddress and caches it; that
-// first call should come before any stream capture. Host code never passes
-// the array's name to a kernel: in host code it names a host-side stand-in,
-// not the device copy.
+// Set-up: every call first resolves the array's device address on the
+// current device with cudaGetSymbolAddress (once per device, cached), even
+// when the request needs no scratch, so the rule is simply that the first
+// call on each device comes before any stream capture. Host code never
+// passes the array's name to a kernel: in host code it names a host-side
+// stand-in, not the device copy. The cached address assumes the device's
+// context lives as long as the process: a cudaDeviceReset after the first
+// call is not supported.
 //
 // Sharing: every call on a device uses the same array and leaves the last
 // call's contents in it. Nothing in it has to start at zero (the repack
-// writes every byte the GEMM then reads, padding included). Calls that
+// writes every byte the GEMM then reads, padding included, and the first
+// pass of a K split writes every partial the second pass reads). Calls that
 // overlap on the GPU (different streams, or several host threads) race on
-// the array: order them on one stream or serialize them.
+// the array, repacks and K-split partials alike: order them on one stream or
+// serialize them.
 #include <mutex>
 
 #include "internal.h"
@@ -77,12 +85,10 @@ extern "C" int choreo_gemm_noalloc(const choreo_gemm_desc* d, void* stream) {
                              "the built-in scratch holds %u bytes. Align the operands (16-byte base and "
                              "leading dimension) or use choreo_gemm with a workspace.",
                              static_cast<long long>(q.workspace_min_bytes), CHOREO_GEMM_NOALLOC_SCRATCH_BYTES);
-  void* scratch = nullptr;
-  size_t scratch_bytes = 0;
-  if (q.workspace_bytes > 0) {
-    scratch = device_scratch();
-    if (scratch == nullptr) return CHOREO_ERR_CUDA;
-    scratch_bytes = CHOREO_GEMM_NOALLOC_SCRATCH_BYTES;
-  }
-  return choreo_gemm(d, scratch, scratch_bytes, stream);
+  // Resolved on every first call per device, needed or not (see set-up above).
+  void* scratch = device_scratch();
+  if (scratch == nullptr) return CHOREO_ERR_CUDA;
+  if (q.workspace_bytes == 0) return choreo_gemm(d, nullptr, 0, stream);
+  // Repacks first, then K-split partials if they fit in the rest.
+  return choreo_gemm(d, scratch, CHOREO_GEMM_NOALLOC_SCRATCH_BYTES, stream);
 }

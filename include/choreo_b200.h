@@ -151,6 +151,32 @@ int choreo_device_props_get(int device, choreo_device_props* out);
  * stream itself reports an error. */
 int choreo_sync_status(void* stream);
 
+/* Process-wide overrides of the dispatcher's choices, for tests and tuning
+ * sweeps. A zeroed struct with l2_policy_a/b = -1 (what choreo_tuning_set(NULL)
+ * installs) leaves every decision to the library; production callers never
+ * need to touch it. Nothing is read from the environment. The reference
+ * exposes the same kind of knob as GEMMConfig::tile_m/n/k and backend
+ * (compute/compute.hpp:32-44), which its dispatcher ignores. */
+typedef struct choreo_tuning {
+  char tile[16];            /* "" = cost model; else force "wide256", "pair256", "pair128",
+                               "single256", "single128" or "single64" (GEMM and conv) */
+  int32_t split_k;          /* 0 = cost model; n >= 1 = only plans with exactly n K ranges
+                               (where K divides into them; else the unsplit plan) */
+  int32_t group_m;          /* 0 = rasterise tiles in groups of 4096 rows of A;
+                               n >= 1 = groups of n M tiles */
+  int32_t l2_policy_a;      /* -1 = default (evict_last); 0 normal, 1 evict_last, 2 evict_first */
+  int32_t l2_policy_b;      /* -1 = default (normal); same codes */
+  double wait_timeout_ms;   /* 0 = default 2000: limit of every bounded pipeline wait */
+} choreo_tuning;
+
+/* Installs *t for every later call from any host thread (NULL restores the
+ * defaults). CHOREO_ERR_INVALID_ARG for an unknown tile name or an out-of-range
+ * field, leaving the previous settings in place. */
+int choreo_tuning_set(const choreo_tuning* t);
+
+/* Copies the settings in force into *out. */
+int choreo_tuning_get(choreo_tuning* out);
+
 /* Launches one CTA that waits, through the bounded wait every kernel
  * pipeline uses, on an mbarrier nothing arrives on. The wait gives up after
  * timeout_ms, records a timeout in the status word and the kernel returns:
@@ -176,8 +202,9 @@ int choreo_gemm_query(const choreo_gemm_desc* d, choreo_launch_config* out);
 int choreo_gemm(const choreo_gemm_desc* d, void* workspace, size_t workspace_bytes,
                 void* stream);
 
-/* Size of the scratch array choreo_gemm_noalloc stages repacked operands in
- * (one per GPU that loads the library, held until the process exits). */
+/* Size of the scratch array choreo_gemm_noalloc stages repacked operands and
+ * K-split partial sums in (one per GPU that loads the library, held until
+ * the process exits). */
 #define CHOREO_GEMM_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 
 /* choreo_gemm for callers that cannot allocate device memory: it takes no
@@ -185,12 +212,16 @@ int choreo_gemm(const choreo_gemm_desc* d, void* workspace, size_t workspace_byt
  * operator* allocates its output with cudaMalloc, tensor/tensor.hpp:671).
  * Callers such as plugins inside a runtime that owns all device buffers, or
  * loops that must not call cudaMalloc (it can synchronize the device and
- * break a pre-planned memory budget), pass only inputs and outputs; an
- * operand that needs repacking (not 16-byte aligned) is staged in the
- * library's built-in scratch array of CHOREO_GEMM_NOALLOC_SCRATCH_BYTES,
- * and a request needing more returns CHOREO_ERR_WORKSPACE. The first call
- * on a device resolves the array's address (make it before any stream
- * capture). All calls on a device share the array: calls that overlap on
+ * break a pre-planned memory budget), pass only inputs and outputs. What
+ * choreo_gemm would keep in its workspace lives in the library's built-in
+ * scratch array of CHOREO_GEMM_NOALLOC_SCRATCH_BYTES instead: the repack of
+ * an operand that is not 16-byte aligned (a request whose repack needs more
+ * returns CHOREO_ERR_WORKSPACE) and, when they fit beside it, the fp32
+ * partials of a K split (a long-K GEMM with few output tiles; when they do
+ * not fit the GEMM runs unsplit). The first call on each device resolves the
+ * array's address, whatever the request: make it before any stream capture;
+ * a cudaDeviceReset after it is not supported. All calls on a device share
+ * the array, aligned operands with a K split included: calls that overlap on
  * the GPU race, so keep them on one stream. */
 int choreo_gemm_noalloc(const choreo_gemm_desc* d, void* stream);
 
@@ -198,7 +229,9 @@ int choreo_gemm_noalloc(const choreo_gemm_desc* d, void* stream);
  * device devices[i]'s slab (its own A rows, its replica of B and bias, its C
  * rows). One host thread per device launches on streams[i] (NULL = default
  * stream) and, if ms_out != NULL, synchronizes and stores that device's
- * kernel time in ms_out[i]. No data crosses between devices. The M-row
+ * kernel time in ms_out[i] (-1 where none was measured: the shard failed).
+ * Returns the first failing shard's status, naming it by index and device
+ * in choreo_last_error(). No data crosses between devices. The M-row
  * split of a large GEMM across the GPUs of one box, B replicated; the
  * reference has no multi-GPU code (core/device.hpp:136-156 only switches
  * devices). */

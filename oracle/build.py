@@ -9,7 +9,11 @@
                                is used if it was shipped, else the pin tests
                                skip and the restatement stands alone.
 
-Usage: python oracle/build.py [-v]
+REFERENCE_ROOT is the reference checkout: `--reference PATH`, else the
+CHOREO_REFERENCE_ROOT environment variable, else a checkout named `reference`
+beside this repository's root directory.
+
+Usage: python oracle/build.py [-v] [--reference PATH]
 """
 from __future__ import annotations
 
@@ -20,7 +24,7 @@ import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REFERENCE_ROOT = Path(os.environ.get("CHOREO_REFERENCE_ROOT", "/root/reference"))
+REFERENCE_ROOT = Path(os.environ.get("CHOREO_REFERENCE_ROOT", str(HERE.parent.parent / "reference")))
 LIB = HERE / "liboracle.so"
 REF_DIR = HERE / "_ref"
 REF_LIB = REF_DIR / "libchoreo_ref.so"
@@ -46,8 +50,8 @@ def build_oracle(verbose: bool = False) -> Path:
     return LIB
 
 
-def build_reference(verbose: bool = False) -> Path | None:
-    inc = REFERENCE_ROOT / "include"
+def build_reference(verbose: bool = False, reference_root: Path | None = None) -> Path | None:
+    inc = Path(reference_root or REFERENCE_ROOT) / "include"
     if not (inc / "choreo-ir" / "choreo-ir.hpp").exists():
         return REF_LIB if REF_LIB.exists() else None
     srcs = [HERE / "ref_entry.cu", HERE / "ref_shim.h"]
@@ -69,11 +73,14 @@ def build_reference(verbose: bool = False) -> Path | None:
     return REF_LIB
 
 
-def build(verbose: bool = False) -> None:
+def build(verbose: bool = False, reference_root: Path | None = None) -> None:
     build_oracle(verbose)
-    build_reference(verbose)
+    build_reference(verbose, reference_root)
 
 
 if __name__ == "__main__":
-    build(verbose="-v" in sys.argv)
+    ref = None
+    if "--reference" in sys.argv:
+        ref = Path(sys.argv[sys.argv.index("--reference") + 1])
+    build(verbose="-v" in sys.argv, reference_root=ref)
     print(LIB, REF_LIB if REF_LIB.exists() else "(reference not built)")

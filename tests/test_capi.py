@@ -48,6 +48,7 @@ def test_struct_layout_matches_c_compiler(cb, tmp_path):
         "choreo_launch_config": cb.LaunchConfig,
         "choreo_conv_desc": cb.ConvDesc,
         "choreo_device_props": cb.DeviceProps,
+        "choreo_tuning": cb.Tuning,
     }
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void) {"]
     for cname, py in structs.items():
@@ -214,3 +215,31 @@ def test_tensor_map_encode_rejects_bad_arguments(cb):
         assert enc(*args) == -1, msg
         assert msg in cb.lib.choreo_last_error().decode(), (msg, cb.lib.choreo_last_error())
     assert enc(m, 3, 2, base, ok_dims, ok_str, ok_box, 0) == -2  # unsupported dtype
+
+
+# ------------------------------------------------------------------ tuning overrides (explicit API, no environment)
+def test_tuning_defaults_roundtrip_and_validation(cb):
+    """choreo_tuning_set / _get: NULL restores the defaults, valid settings
+    round-trip, invalid ones are refused and leave the previous settings."""
+    assert cb.lib.choreo_tuning_set(None) == 0
+    d = cb.get_tuning()
+    assert (d.tile, d.split_k, d.group_m, d.l2_policy_a, d.l2_policy_b, d.wait_timeout_ms) == (b"", 0, 0, -1, -1, 0.0)
+    with cb.tuning(tile="single128", split_k=4, group_m=8, l2_policy_a=2, l2_policy_b=1, wait_timeout_ms=250.0):
+        t = cb.get_tuning()
+        assert (t.tile, t.split_k, t.group_m, t.l2_policy_a, t.l2_policy_b, t.wait_timeout_ms) == \
+            (b"single128", 4, 8, 2, 1, 250.0)
+        for bad, msg in [(dict(tile="huge512"), "unknown tile"), (dict(split_k=65), "split_k"),
+                         (dict(group_m=-1), "group_m"), (dict(l2_policy_a=3), "L2 policy"),
+                         (dict(wait_timeout_ms=-1.0), "wait_timeout_ms")]:
+            with pytest.raises(cb.ChoreoError, match=msg):
+                cb.set_tuning(**bad)
+        assert cb.get_tuning().tile == b"single128"  # unchanged by the refused calls
+    assert cb.get_tuning().tile == b""
+
+
+def test_library_reads_no_environment():
+    """The dispatcher's knobs are an explicit API: no source of the library
+    calls getenv, so a stray variable in a caller's environment changes
+    nothing."""
+    for f in (ROOT / "choreo-ir_b200" / "csrc").glob("*.cu*"):
+        assert "getenv" not in f.read_text(), f.name

@@ -101,13 +101,13 @@ def test_conv_query(cb, cuda):
 
 
 @pytest.mark.parametrize("tile", ["wide256", "pair256", "pair128", "single256", "single128", "single64"])
-def test_conv_forced_tiles(cb, cuda, orc, monkeypatch, tile):
-    monkeypatch.setenv("CHOREO_GEMM_TILE", tile)
+def test_conv_forced_tiles(cb, cuda, orc, tile):
     x = orc.to_bits(orc.uniform((3, 13, 11, 128), 0, 1, 7), F16)
     wt = orc.to_bits(orc.normal((192, 3, 3, 128), 0, 1.0 / 34, 8), F16)
     bias = orc.normal((192,), 0, 0.1, 9)
-    out = run_conv(cb, to_dev(x, F16), to_dev(wt, F16), F16, bias=to_dev(bias, F32), relu=True)
-    q = cb.conv2d_query(cb.conv_desc(to_dev(x, F16), to_dev(wt, F16), out))
+    with cb.tuning(tile=tile):
+        out = run_conv(cb, to_dev(x, F16), to_dev(wt, F16), F16, bias=to_dev(bias, F32), relu=True)
+        q = cb.conv2d_query(cb.conv_desc(to_dev(x, F16), to_dev(wt, F16), out))
     assert q.cluster_m == (2 if tile.startswith(("pair", "wide")) else 1)
     ref = orc.conv2d_f64(x, wt, F16, bias=bias, dtype_bias=F32, relu=True)
     assert_close(as_f64(to_host(out), F16).reshape(-1, 192), ref, what=f"conv {tile}", k=9 * 128)

@@ -177,6 +177,47 @@ def test_rowsharded_65536x8192x8192_full_and_slabs(cb, cuda, orc):
     del c
 
 
+@pytest.mark.parametrize("nshards", [1, 2, 3])
+def test_rowsharded_driver_on_device0(cb, cuda, orc, nshards):
+    """choreo_gemm_rowsharded, the one-process multi-GPU driver, with every
+    shard on device 0 (one host thread and one stream per shard): the rows
+    match the fp64 oracle, each shard matches the same descriptor run alone
+    through choreo_gemm bit for bit, and every shard reports its kernel time."""
+    import ctypes as C
+    import torch
+    M, N, K = 1000, 384, 640
+    a = dev_uniform((M, K), -0.5, 0.5, 51, BF16)
+    b = dev_uniform((K, N), -0.5, 0.5, 52, BF16)
+    bias = dev_normal((N,), 0, 0.1, 53, BF16)
+    c = torch.full((M, N), 9.0, device="cuda", dtype=torch.bfloat16)
+    spans = [cb.shard_rows(M, nshards, r) for r in range(nshards)]
+    descs = (cb.GemmDesc * nshards)(*[cb.make_gemm_desc(a[r0:r0 + rows], b, c[r0:r0 + rows], m=rows, n=N, k=K,
+                                                        bias=bias, relu=True) for r0, rows in spans])
+    devices = (C.c_int * nshards)(*([0] * nshards))
+    streams = [torch.cuda.Stream() for _ in range(nshards)]
+    sptrs = (C.c_void_p * nshards)(*[s.cuda_stream for s in streams])
+    ms = (C.c_float * nshards)(*([-5.0] * nshards))
+    torch.cuda.synchronize()
+    cb.check(cb.lib.choreo_gemm_rowsharded(descs, nshards, devices, sptrs, ms))
+    torch.cuda.synchronize()
+    cb.sync_status()
+    assert all(0.0 < v < 1000.0 for v in ms), list(ms)
+    r = orc.gemm_f64(to_host(a), to_host(b), BF16, bias=to_host(bias), dtype_bias=BF16, relu=True)
+    assert_close(as_f64(to_host(c), BF16), r, what=f"rowsharded x{nshards}", k=K)
+    alone = torch.full_like(c, 9.0)
+    for r0, rows in spans:
+        cb.gemm_desc(cb.make_gemm_desc(a[r0:r0 + rows], b, alone[r0:r0 + rows], m=rows, n=N, k=K, bias=bias,
+                                       relu=True))
+    cb.sync_status()
+    assert torch.equal(c, alone)
+    # untimed form (ms_out = NULL) on the default streams
+    c.fill_(9.0)
+    torch.cuda.synchronize()
+    cb.check(cb.lib.choreo_gemm_rowsharded(descs, nshards, devices, None, None))
+    torch.cuda.synchronize()
+    assert torch.equal(c, alone)
+
+
 # ------------------------------------------------------------------ the 32x56x56x256 3x3 conv lives in test_conv_gpu.py
 
 # ------------------------------------------------------------------ edge cases
@@ -299,10 +340,15 @@ TILES = ["wide256", "pair256", "pair128", "single256", "single128", "single64"]
 
 
 @pytest.fixture
-def force_tile(monkeypatch):
+def force_tile(cb):
+    """Forces a tile shape through the tuning API for one test, then restores
+    the previous settings."""
+    saved = cb.get_tuning()
+
     def _set(name):
-        monkeypatch.setenv("CHOREO_GEMM_TILE", name)
-    return _set
+        cb.set_tuning(tile=name)
+    yield _set
+    cb.check(cb.lib.choreo_tuning_set(cb.C.byref(saved)))
 
 
 @pytest.mark.parametrize("tile", TILES)

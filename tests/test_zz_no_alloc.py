@@ -92,6 +92,32 @@ def test_noalloc_aligned_operands_need_no_scratch(cb, cuda, orc):
     compare(orc, c_new, c_old)
 
 
+def test_noalloc_split_k_partials_in_scratch(cb, cuda, orc):
+    """Aligned operands, few output tiles over a long K: the planner splits K
+    and the fp32 partial sums live in the built-in scratch. Two calls in a
+    row (the second sees the first's partials left in the array) agree with
+    choreo_gemm given its own workspace and with the fp64 oracle."""
+    import torch
+    from _util import as_f64, to_host
+    m, n, k = 300, 200, 8192
+    for call, seed in enumerate((81, 83)):
+        a = dev_uniform((m, k), -1, 1, seed, F16)
+        b = dev_uniform((k, n), -1, 1, seed + 1, F16)
+        bias = dev_normal((n,), 0, 0.1, seed + 2, F16)
+        c_new = torch.full((m, n), 7.0, device="cuda", dtype=torch.float16)
+        c_old = torch.full((m, n), 7.0, device="cuda", dtype=torch.float16)
+        d_new = cb.make_gemm_desc(a, b, c_new, m=m, n=n, k=k, bias=bias, relu=True)
+        d_old = cb.make_gemm_desc(a, b, c_old, m=m, n=n, k=k, bias=bias, relu=True)
+        q = cb.gemm_query(d_new)
+        assert q.split_k > 1 and q.workspace_min_bytes == 0, (call, q.split_k)
+        assert 0 < q.workspace_bytes <= SCRATCH_BYTES
+        noalloc_entry(cb, d_new)
+        existing_entry(cb, d_old)
+        compare(orc, c_new, c_old)
+        r = orc.gemm_f64(to_host(a), to_host(b), F16, bias=to_host(bias), dtype_bias=F16, relu=True)
+        assert orc.rel_err(as_f64(to_host(c_new), F16), r, k) <= TOL
+
+
 def test_noalloc_rejects_repack_larger_than_scratch(cb, cuda):
     import torch
     M, N, K = 4097, 64, 8192  # A^T repack: 8192 x 4104 x 2 bytes = 67 MB > 32 MiB
