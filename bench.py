@@ -1,18 +1,17 @@
 """Benchmark of the dense-contraction path on B200; prints ONE JSON line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl choreo|reference]
-                    [--workload auto|gemm8192|sharded|custom|smallk|conv|relu]
+                    [--workload auto|sharded|gemm8192|custom|smallk|conv|relu]
 
 Workloads (inputs are seeded synthetic data of the configuration's shapes and
 distributions; nothing is read from disk):
-  gemm8192  fp16 GEMM C[8192x8192] = A[8192x8192] B[8192x8192], row-major,
-            U[-1,1], fp32 accumulation, fp16 output. The default at N = 1.
   sharded   row-sharded bf16 GEMM M=65536, N=K=8192, U[-0.5,0.5], bias ~N(0,0.1)
             fused with ReLU, bf16 output; rows split across the N ranks
             (strong scaling: total work fixed), B and bias replicated, no
-            collective on the data path. The default at N > 1; there the
-            replication of B from rank 0 and the gather of the C slabs onto
-            rank 0 are timed apart over NCCL (config.exchanges_outside_timing).
+            collective on the data path. The default at every N, N = 1
+            included, so the 1 -> N curve compares one workload.
+  gemm8192  fp16 GEMM C[8192x8192] = A[8192x8192] B[8192x8192], row-major,
+            U[-1,1], fp32 accumulation, fp16 output.
   custom    GEMM of --shape MxNxK and --dtype (U[-1,1], NN).
   smallk    fp16 GEMM 16384 x 16384 x 128: output-write (HBM) bound.
   conv      implicit-GEMM conv2d NHWC fp16, N=32, 56x56, C=K=256, 3x3, s1 p1,
@@ -26,16 +25,24 @@ value : whole-job throughput with inputs resident in HBM; K steps timed with
         max over ranks. Where the inputs fit in the 126 MB L2 (conv, smallk),
         a 256 MB buffer is written between steps and each launch is timed by
         its own event pair; elsewhere the inputs exceed the L2.
-e2e   : the same metric through the C ABI with pinned HOST buffers: every step
-        copies the inputs host->device, runs the launch and copies the output
-        back, all inside the timed region (GEMMs through choreo_b200.HostGemmPlan,
-        which overlaps the copies of one row slab with the GEMM of another).
+e2e   : the same metric through the C ABI's host-buffer plans
+        (choreo_host_gemm_run / choreo_host_conv_run) with pinned HOST
+        buffers: every step copies the inputs host->device, runs the launches
+        and copies the output back, all inside the timed region. For the
+        sharded GEMM at N > 1, B crosses PCIe once per step in total: each rank
+        copies 1/N of B's rows and an NCCL all-gather over NVLink assembles B
+        on every rank (inside the timed region).
+configs : at N = 1, every other configuration of the benchmark suite (1024 x
+        1024 x 512; 2048/4096/8192 cubes in f16 and bf16; 4097 x 3000 x 1536 in
+        NN/NT/TN; the 3x3 conv; small-K) timed the same way, with cuBLAS /
+        cuDNN (through torch) on the same GPU as a side reference.
 cpu_baseline : the reference's own CPU path (operator*, relu from
         include/choreo-ir/choreo-ir.hpp, compiled from its sources into
-        oracle/_ref) on a bounded sample, on the host's cores; the oracle's C
-        restatement where the reference library is absent or has no such
-        entry (conv: the loop of benchmark/kernels/gemm_example.cu:208-253).
---impl reference : that reference CPU path alone, as the comparison arm.
+        oracle/_ref) on a bounded sample, on all of the host's cores; the
+        oracle's C restatement where the reference library is absent or has no
+        such entry (conv: the loop of benchmark/kernels/gemm_example.cu:208-253).
+--impl reference : that reference CPU path alone, as the comparison arm (rank
+        0 only under torchrun; same `config` block as this arm's).
 """
 from __future__ import annotations
 
@@ -68,12 +75,21 @@ def load_choreo():
     return mod
 
 
-def _gemm(workload, m, n, k, dtype, dist, bias, relu):
+def host_cores() -> int:
+    """Host threads this process may run on (the affinity mask, not
+    OMP_NUM_THREADS, which torchrun sets to 1 for every rank)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def _gemm(workload, m, n, k, dtype, dist, bias, relu, layout="NN"):
     return dict(kind="gemm", workload=workload, m_total=m, n=n, k=k, dtype=dtype, dist=dist, bias=bias,
-                relu=relu, layout="NN")
+                relu=relu, layout=layout)
 
 
-def workload_spec(name: str, world: int, shape: str | None = None, dtype: str = "f16") -> dict:
+def workload_spec(name: str, shape: str | None = None, dtype: str = "f16") -> dict:
     if name == "custom":
         m, n, k = (int(x) for x in (shape or "4096x4096x4096").lower().split("x"))
         return _gemm(f"gemm_{dtype}_{m}x{n}x{k}", m, n, k, dtype, "U[-1,1]", False, False)
@@ -97,13 +113,75 @@ def spec_flops_bytes(spec: dict, rows: int | None = None) -> tuple[float, float]
     if spec["kind"] == "gemm":
         m = rows if rows is not None else spec["m_total"]
         n, k = spec["n"], spec["k"]
-        return 2.0 * m * n * k, 2.0 * (m * k + k * n + m * n) + (2.0 * n if spec["bias"] else 0.0)
+        ob = 2.0
+        return 2.0 * m * n * k, 2.0 * (m * k + k * n) + ob * m * n + (2.0 * n if spec["bias"] else 0.0)
     if spec["kind"] == "conv":
         npix = spec["n"] * spec["h"] * spec["w"]          # stride 1, same padding
         red = spec["r"] * spec["s"] * spec["c"]
         return (2.0 * npix * spec["k"] * red,
                 2.0 * (npix * spec["c"] + spec["k"] * red + npix * spec["k"] + spec["k"]))
     return 0.0, 4.0 * spec["numel"]
+
+
+def shard_rows(m: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows of an m-row problem rank `rank` of `world` owns: the partition of
+    choreo_shard_rows (whole 128-row tiles, counts differing by at most one
+    tile), restated so the reference arm needs no GPU library."""
+    tiles = (m + 127) // 128
+    base, extra = divmod(tiles, world)
+    t0 = rank * base + min(rank, extra)
+    nt = base + (1 if rank < extra else 0)
+    r0, r1 = min(t0 * 128, m), min((t0 + nt) * 128, m)
+    return r0, r1 - r0
+
+
+def conv_images(n: int, world: int, rank: int) -> tuple[int, int]:
+    """This rank's contiguous run of images (first, count): the batch split
+    evenly, the first n % world ranks taking one extra."""
+    base, extra = divmod(n, world)
+    count = base + (1 if rank < extra else 0)
+    return rank * base + min(rank, extra), count
+
+
+def flushes_l2(spec: dict, world: int) -> bool:
+    """Inputs of rank 0's launch fit in the L2: the timing flushes it."""
+    if spec["kind"] == "gemm":
+        _, rows = shard_rows(spec["m_total"], world, 0)
+        fl, by = spec_flops_bytes(spec, rows)
+        return by - 2.0 * rows * spec["n"] <= L2_BYTES
+    if spec["kind"] == "conv":
+        _, imgs = conv_images(spec["n"], world, 0)
+        _, by = spec_flops_bytes({**spec, "n": imgs})
+        return by - 2.0 * imgs * spec["h"] * spec["w"] * spec["k"] <= L2_BYTES
+    return False
+
+
+def config_block(spec: dict, world: int) -> dict:
+    """The workload's `config`: a function of the workload and the GPU count
+    only, so the reference arm prints the very same block."""
+    l2 = ("L2 flushed (256 MB written) between timed launches; per-launch events" if flushes_l2(spec, world)
+          else "inputs larger than the 126 MB L2 (no flush needed)")
+    if spec["kind"] == "gemm":
+        _, rows = shard_rows(spec["m_total"], world, 0)
+        return {"workload": spec["workload"], "m": spec["m_total"], "n": spec["n"], "k": spec["k"],
+                "layout": spec["layout"],
+                "inputs": f"{spec['dist']} seeded; fp32 accumulation; {spec['dtype']} output",
+                "epilogue": "bias+ReLU" if spec["bias"] else "none",
+                "parallelism": (f"row-sharded over {world} GPU(s), B replicated, no collective on the data path"
+                                if world > 1 else "single GPU"),
+                "rows_per_rank": rows, "l2": l2}
+    if spec["kind"] == "conv":
+        _, imgs = conv_images(spec["n"], world, 0)
+        return {"workload": spec["workload"], "n": spec["n"], "h": spec["h"], "w": spec["w"], "c": spec["c"],
+                "k": spec["k"], "rs": f"{spec['r']}x{spec['s']}", "stride": spec["stride"], "pad": spec["pad"],
+                "inputs": "activations U[0,1], weights N(0,1/48), bias N(0,0.1), seeded; fp32 accumulation; "
+                          "fp16 output",
+                "epilogue": "bias+ReLU",
+                "parallelism": "single GPU" if world == 1 else
+                f"batch split over {world} GPUs, weights replicated, no collective",
+                "images_per_rank": imgs, "l2": l2}
+    return {"workload": spec["workload"], "numel": spec["numel"], "inputs": "U[-1,1] seeded",
+            "parallelism": "single GPU" if world == 1 else f"{world} independent replicas", "l2": l2}
 
 
 def measured_peaks() -> dict:
@@ -216,17 +294,17 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------- reference CPU path
-def reference_cpu_sample(spec: dict, seconds_target: float, nthreads: int | None = None) -> dict:
+def reference_cpu_sample(spec: dict, seconds_target: float, nthreads: int) -> dict:
     """A bounded sample of the workload for the reference CPU path, sized so
-    one call takes about `seconds_target`:
-      gemm: `rows` rows of A (one per thread) against a column slice of B;
-            per element the arithmetic is the reference operator*'s (16-bit
-            accumulation in k order);
+    one call takes about `seconds_target` on `nthreads` host threads:
+      gemm: `rows` rows of A (a multiple of the thread count) against a column
+            slice of B; per element the arithmetic is the reference
+            operator*'s (16-bit accumulation in k order);
       conv: a run of output pixels through the reference conv loop;
       relu: a prefix of the tensor through the reference relu.
     Returns the inputs plus `units` (FLOPs, or bytes for relu) per call."""
     from oracle import oracle as orc
-    threads = nthreads or orc.threads()
+    threads = max(1, nthreads)
     if spec["kind"] == "gemm":
         dt = F16 if spec["dtype"] == "f16" else BF16
         lo, hi = (-1.0, 1.0) if spec["dist"] == "U[-1,1]" else (-0.5, 0.5)
@@ -319,11 +397,15 @@ def metric_of(spec: dict) -> tuple[str, str]:
     return f"GEMM TFLOP/s ({spec['workload']})", "TFLOP/s"
 
 
+def scaling_of(spec: dict, world: int) -> str:
+    return "strong" if world > 1 and (spec.get("m_total") == 65536 or spec["kind"] == "conv") else "weak"
+
+
 def bench_reference(args, spec: dict, world: int, rank: int) -> None:
     if rank != 0:
         return
     metric, unit = metric_of(spec)
-    s = reference_cpu_sample(spec, seconds_target=float(os.environ.get("CHOREO_REF_STEP_SECONDS", "1.0")))
+    s = reference_cpu_sample(spec, float(os.environ.get("CHOREO_REF_STEP_SECONDS", "1.0")), host_cores())
     for _ in range(args.warmup):
         run_reference_sample(s)
     times = [run_reference_sample(s) for _ in range(args.steps)]
@@ -333,9 +415,10 @@ def bench_reference(args, spec: dict, world: int, rank: int) -> None:
     line = {
         "metric": metric, "value": value, "unit": unit, "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
-        "higher_is_better": True, "scaling": "strong" if spec.get("m_total") == 65536 else "weak",
+        "higher_is_better": True, "scaling": scaling_of(spec, world),
         "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic",
-        "config": {**spec, "timed": "CPU wall clock per step over a bounded sample"},
+        "config": config_block(spec, world),
+        "timing": "CPU wall clock per step over a bounded sample of the workload",
         "cpu_baseline": {"value": value, "unit": unit, "cores": s["threads"],
                          "kind": "reference" if s["use_ref"] else "port", "sample": sample_text(s, spec)},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -353,7 +436,8 @@ class Case:
     flops = bytes_ = 0.0  # this rank's algorithmic FLOPs / bytes per launch
     flush = False      # inputs + outputs fit in L2: flush between timed launches
     launches_per_step = 1
-    info: dict = {}
+    kernel: dict = {}  # what the dispatcher chose
+    e2e_info: dict = {}
 
 
 def _pinned_copy(t):
@@ -363,8 +447,22 @@ def _pinned_copy(t):
     return h
 
 
+def kernel_name(q) -> str:
+    if q.kernel == 3 or q.kernel == 1:
+        if q.cluster_m == 2 and q.tile_m == 512:
+            base = "tc_gemm_pair_wide_kernel"
+        elif q.cluster_m == 2:
+            base = "tc_gemm_pair_kernel"
+        else:
+            base = "tc_gemm_kernel"
+        return f"{base} ({q.tile_m}x{q.tile_n}x{q.tile_k} tile{', CTA pair' if q.cluster_m == 2 else ''}" + \
+               (f", K split {q.split_k} + splitk_reduce_kernel" if q.split_k > 1 else "") + ")"
+    return "gemm_f32_kernel"
+
+
 def setup_gemm(cb, spec, world, rank, dev, stream) -> Case:
     import torch
+    import torch.distributed as dist
     dt = torch.float16 if spec["dtype"] == "f16" else torch.bfloat16
     lo, hi = (-1.0, 1.0) if spec["dist"] == "U[-1,1]" else (-0.5, 0.5)
     M_total, N, K = spec["m_total"], spec["n"], spec["k"]
@@ -389,34 +487,45 @@ def setup_gemm(cb, spec, world, rank, dev, stream) -> Case:
     bias_h = _pinned_copy(bias) if bias is not None else None
     c_h = torch.empty(rows, N, dtype=dt, pin_memory=True)
     plan = cb.HostGemmPlan(rows, N, K, dt, bias=bias is not None, relu=spec["relu"], device=dev)
-    case.e2e_step = lambda: plan.run(a_h, b_h, c_h, bias_h, stream=stream)
-    case.h2d = sum(t.numel() * t.element_size() for t in (a_h, b_h, bias_h) if t is not None)
+    if world == 1:
+        # one process: the plan copies B and the bias in before the row slabs
+        case.e2e_step = lambda: plan.run(a_h, b_h, c_h, bias_h, stream=stream)
+        case.h2d = sum(t.numel() * t.element_size() for t in (a_h, b_h, bias_h) if t is not None)
+        case.e2e_info = {"path": f"choreo_host_gemm_run: pinned host A/B/bias in, C out; {plan.launches()} row "
+                                 "slabs, copies in, GEMMs and copies out overlapped on three streams"}
+    else:
+        # B crosses PCIe once for the whole job: each rank copies 1/world of
+        # B's rows, and an NCCL all-gather over NVLink assembles B everywhere.
+        share = -(-K // world)
+        b_full = torch.empty(share * world, N, device=dev, dtype=dt)
+        b_part = torch.empty(share, N, device=dev, dtype=dt)
+        k0, k1 = min(rank * share, K), min((rank + 1) * share, K)
+        bias_d = torch.empty_like(bias) if bias is not None else None
+
+        def e2e():
+            if k1 > k0:
+                b_part[:k1 - k0].copy_(b_h[k0:k1], non_blocking=True)
+            if bias_d is not None:
+                bias_d.copy_(bias_h, non_blocking=True)
+            dist.all_gather_into_tensor(b_full, b_part)
+            plan.run(a_h, b_full, c_h, bias_d, stream=stream, operands_on_device=True)
+
+        case.e2e_step = e2e
+        case.h2d = a_h.numel() * a_h.element_size() + (k1 - k0) * N * b_h.element_size() + \
+            (bias_h.numel() * bias_h.element_size() if bias_h is not None else 0)
+        case.e2e_info = {"path": f"choreo_host_gemm_run with B on the device: pinned host A slab in, C slab out; "
+                                 f"{plan.launches()} row slabs overlapped on three streams; B assembled per step "
+                                 f"from {share} host rows per rank by an NCCL all-gather (inside the timed "
+                                 f"region); bias copied in per step"}
     case.d2h = c_h.numel() * c_h.element_size()
     case.rows = rows
     case.b_dev, case.c_dev = b, c
     case.flops, case.bytes_ = spec_flops_bytes(spec, rows)
     case.units_total = spec_flops_bytes(spec)[0]
-    case.flush = case.bytes_ - 2.0 * rows * N <= L2_BYTES      # A + B (+ bias) fit in L2
-    case.info = {
-        "m": M_total, "n": N, "k": K, "layout": spec["layout"],
-        "inputs": f"{spec['dist']} seeded on device; fp32 accumulation; {spec['dtype']} output",
-        "split_k": int(q.split_k),
-        "epilogue": "bias+ReLU" if spec["bias"] else "none",
-        "parallelism": f"row-sharded over {world} GPU(s), B replicated, no collective" if world > 1 else "single GPU",
-        "rows_per_rank": rows, "tile": f"{q.tile_m}x{q.tile_n}x{q.tile_k}", "cluster": q.cluster_m,
-        "stages": q.stages, "grid": q.grid_x,
-        "e2e": f"HostGemmPlan: pinned host A/B/bias in, C out; {plan.launches()} row slabs, copies in, GEMMs "
-               "and copies out on three streams",
-    }
+    case.flush = flushes_l2(spec, world)
+    case.kernel = {"name": kernel_name(q), "tile": f"{q.tile_m}x{q.tile_n}x{q.tile_k}", "cluster": q.cluster_m,
+                   "stages": q.stages, "grid": q.grid_x, "split_k": int(q.split_k)}
     return case
-
-
-def conv_images(n: int, world: int, rank: int) -> tuple[int, int]:
-    """This rank's contiguous run of images (first, count): the batch split
-    evenly, the first n % world ranks taking one extra."""
-    base, extra = divmod(n, world)
-    count = base + (1 if rank < extra else 0)
-    return rank * base + min(rank, extra), count
 
 
 def setup_conv(cb, spec, world, rank, dev, stream) -> Case:
@@ -446,18 +555,11 @@ def setup_conv(cb, spec, world, rank, dev, stream) -> Case:
     case.d2h = o_h.numel() * o_h.element_size()
     case.flops, case.bytes_ = spec_flops_bytes({**spec, "n": imgs})
     case.units_total = spec_flops_bytes(spec)[0]
-    case.flush = case.bytes_ - 2.0 * out.numel() <= L2_BYTES    # activations + weights fit in L2
-    case.info = {"n": spec["n"], "h": spec["h"], "w": spec["w"], "c": spec["c"], "k": spec["k"],
-                 "rs": f"{spec['r']}x{spec['s']}", "stride": spec["stride"], "pad": spec["pad"],
-                 "inputs": "activations U[0,1], weights N(0,1/48), bias N(0,0.1), seeded on device; "
-                           "fp32 accumulation; fp16 output",
-                 "epilogue": "bias+ReLU", "parallelism": "single GPU" if world == 1 else
-                 f"batch split over {world} GPUs ({imgs} images on rank {rank}), weights replicated, "
-                 "no collective",
-                 "tile": f"{q.tile_m}x{q.tile_n}x{q.tile_k}", "cluster": q.cluster_m, "stages": q.stages,
-                 "grid": q.grid_x,
-                 "e2e": f"HostConvPlan: pinned host activations/weights/bias in, output out; {plan.launches()} "
-                        "runs of images, copies in, convolutions and copies out on three streams"}
+    case.flush = flushes_l2(spec, world)
+    case.kernel = {"name": kernel_name(q), "tile": f"{q.tile_m}x{q.tile_n}x{q.tile_k}", "cluster": q.cluster_m,
+                   "stages": q.stages, "grid": q.grid_x}
+    case.e2e_info = {"path": f"choreo_host_conv_run: pinned host activations/weights/bias in, output out; "
+                             f"{plan.launches()} runs of images overlapped on three streams"}
     return case
 
 
@@ -481,8 +583,8 @@ def setup_relu(cb, spec, world, rank, dev, stream) -> Case:
     case.h2d = case.d2h = x_h.numel() * 2
     case.flops, case.bytes_ = spec_flops_bytes(spec)
     case.units_total = case.bytes_ * world
-    case.info = {"numel": spec["numel"], "inputs": "U[-1,1] seeded on device",
-                 "parallelism": "single GPU" if world == 1 else f"{world} independent replicas"}
+    case.kernel = {"name": "map_kernel (relu)"}
+    case.e2e_info = {"path": "torch copies around choreo_relu"}
     return case
 
 
@@ -527,6 +629,115 @@ def time_exchanges(case, world: int, rank: int, dev, stream) -> dict:
     return out
 
 
+class Flusher:
+    """Writes a buffer twice the L2's size between timed launches."""
+
+    def __init__(self, dev):
+        import torch
+        self.buf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        self.buf.fill_(1.0)
+
+
+def median_launch_ms(fn, stream, flush, reps: int, warmup: int = 3) -> float:
+    """Median device time of one call of fn, each call bracketed by its own
+    events on `stream`, the L2 overwritten between calls (outside the events)."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for s, e in evs:
+        flush()
+        s.record(stream)
+        fn()
+        e.record(stream)
+    evs[-1][1].synchronize()
+    return statistics.median(s.elapsed_time(e) for s, e in evs)
+
+
+def run_configs(cb, dev, stream, reps: int) -> list[dict]:
+    """The other configurations of the benchmark suite on this GPU, each timed
+    through the C ABI as the median of `reps` L2-flushed launches, next to
+    cuBLAS / cuDNN (through torch) on the same inputs as a side reference."""
+    import torch
+    import torch.nn.functional as Fn
+    peak, peak_src = measured_peak(0.0)
+    hbm, _ = measured_hbm()
+    flush = Flusher(dev)
+    out = []
+
+    def gemm_entry(name, cfg, m, n, k, dt, layout, dist):
+        g = torch.Generator(device=dev)
+        g.manual_seed(m + 3 * n + 7 * k)
+        tdt = torch.float16 if dt == "f16" else torch.bfloat16
+
+        def gen(shape):
+            t = torch.empty(shape, device=dev)
+            (t.uniform_(-1, 1, generator=g) if dist == "U[-1,1]" else t.normal_(0, 1, generator=g))
+            return t.to(tdt)
+        ta, tb = layout[0] == "T", layout[1] == "T"
+        a = gen((k, m) if ta else (m, k))
+        b = gen((n, k) if tb else (k, n))
+        c = torch.empty(m, n, device=dev, dtype=tdt)
+        d = cb.make_gemm_desc(a, b, c, m=m, n=n, k=k, trans_a=ta, trans_b=tb, lda=a.stride(0), ldb=b.stride(0))
+        q = cb.gemm_query(d)
+        ws = torch.empty(max(1, q.workspace_bytes), dtype=torch.uint8, device=dev)
+        ms = median_launch_ms(lambda: cb.gemm_desc(d, ws, q.workspace_bytes, stream=stream), stream, flush, reps)
+        cb.sync_status(stream)
+        opa = a.t() if ta else a
+        opb = b.t() if tb else b
+        ms_ref = median_launch_ms(lambda: torch.matmul(opa, opb), stream, flush, reps)
+        flops = 2.0 * m * n * k
+        byts = 2.0 * (m * k + k * n + m * n)
+        tf = flops / (ms * 1e-3) / 1e12
+        bound = "tensor" if flops / byts > peak * 1e12 / (hbm * 1e9) else "hbm"
+        e = {"config": cfg, "workload": f"gemm_{dt}_{m}x{n}x{k}_{layout}", "inputs": dist, "kernel": kernel_name(q),
+             "launches": 2 if q.split_k > 1 else 1 + (1 if q.workspace_min_bytes else 0),
+             "us": round(ms * 1e3, 2), "tflops": round(tf, 1), "gbs": round(byts / (ms * 1e-3) / 1e9, 1),
+             "bound": bound,
+             "frac": round(tf / peak, 4) if bound == "tensor" else round(byts / (ms * 1e-3) / 1e9 / hbm, 4),
+             "side_reference": {"what": "cuBLAS via torch.matmul, same inputs and layout", "us": round(ms_ref * 1e3, 2),
+                                "tflops": round(flops / (ms_ref * 1e-3) / 1e12, 1)},
+             "time_vs_side_reference": round(ms / ms_ref, 3)}
+        out.append(e)
+        del a, b, c, ws
+
+    gemm_entry("1", 1024, 1024, 512, "f16", "NN", "U[-1,1]")
+    for s in (2048, 4096, 8192):
+        for dt in ("f16", "bf16"):
+            gemm_entry("2", s, s, s, dt, "NN", "U[-1,1]")
+    for layout in ("NN", "NT", "TN"):
+        gemm_entry("3", 4097, 3000, 1536, "f16", layout, "N(0,1)")
+    gemm_entry("small-K", 16384, 16384, 128, "f16", "NN", "U[-1,1]")
+
+    # config 5: the conv, against cuDNN (channels-last fp16 conv with bias; cuDNN's ReLU is a separate op)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    x = torch.empty(32, 56, 56, 256, device=dev).uniform_(0, 1, generator=g).half()
+    wt = torch.empty(256, 3, 3, 256, device=dev).normal_(0, 1 / 48.0, generator=g).half()
+    bias = torch.empty(256, device=dev).normal_(0, 0.1, generator=g).half()
+    o = torch.empty(32, 56, 56, 256, device=dev, dtype=torch.float16)
+    d = cb.conv_desc(x, wt, o, stride=1, padding=1, bias=bias, relu=True)
+    q = cb.conv2d_query(d)
+    ms = median_launch_ms(lambda: cb.conv2d_desc(d, stream=stream), stream, flush, reps)
+    cb.sync_status(stream)
+    xc = x.permute(0, 3, 1, 2)       # NCHW view of the NHWC data (channels-last)
+    wc = wt.permute(0, 3, 1, 2)      # KCRS view of KRSC
+    ms_ref = median_launch_ms(lambda: Fn.conv2d(xc, wc, bias, stride=1, padding=1), stream, flush, reps)
+    flops = 2.0 * 32 * 56 * 56 * 256 * 2304
+    tf = flops / (ms * 1e-3) / 1e12
+    out.append({"config": "5", "workload": "conv2d_f16_n32_56x56_c256_k256_3x3_bias_relu", "kernel": kernel_name(q),
+                "launches": 1, "us": round(ms * 1e3, 2), "tflops": round(tf, 1), "bound": "tensor",
+                "frac": round(tf / peak, 4),
+                "side_reference": {"what": "cuDNN via torch conv2d, channels-last fp16, bias, no ReLU",
+                                   "us": round(ms_ref * 1e3, 2), "tflops": round(flops / (ms_ref * 1e-3) / 1e12, 1)},
+                "time_vs_side_reference": round(ms / ms_ref, 3)})
+    for e in out:
+        e["peak_source"] = peak_src if e["bound"] == "tensor" else "measured (copy)"
+    return out
+
+
 def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> None:
     import torch
     import torch.distributed as dist
@@ -535,6 +746,8 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     stream = torch.cuda.current_stream(dev)
+    if args.tile:
+        cb.set_tuning(tile=args.tile)
     setup = {"gemm": setup_gemm, "conv": setup_conv, "relu": setup_relu}[spec["kind"]]
     case = setup(cb, spec, world, rank, dev, stream)
     metric, unit = metric_of(spec)
@@ -544,6 +757,7 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
         hbm_gbs = measured_hbm()[0]
         hbm_bound = case.flops / case.bytes_ < peak_tf * 1e12 / (hbm_gbs * 1e9)
     flush_buf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if case.flush else None
+    probe = torch.zeros(3, dtype=torch.int64, device=dev)
 
     def barrier():
         if world > 1:
@@ -582,13 +796,16 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
         sampler.start()
         time.sleep(0.3)
     barrier()
+    cb.check(cb.lib.choreo_clock_probe_set(probe.data_ptr()))
     t_wall0 = time.time()
     ms = timed(case.step, args.steps)
     barrier()
     t_wall1 = time.time()
+    cb.check(cb.lib.choreo_clock_probe_set(None))
     cb.sync_status(stream)
     if sampler:
         sampler.mark(t_wall0, t_wall1)
+    clk = [int(v) for v in probe.cpu()]
 
     # ---------------------------------------------------------- end to end from pinned host buffers
     e2e_steps = max(1, min(args.steps, 20))
@@ -635,21 +852,25 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
     roof["peak_source"] = peak_src
     roof["traffic"] = profiled_traffic(spec["workload"], case.rows)
     roof["per_launch_ms"] = per_launch_ms
+    roof["kernel"] = case.kernel.get("name")
+
+    configs = None
+    if world == 1 and not args.no_configs:
+        configs = run_configs(cb, dev, stream, reps=max(5, min(args.steps, 20)))
 
     if rank != 0:
         return
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        s = reference_cpu_sample(spec, seconds_target=float(os.environ.get("CHOREO_CPU_BASELINE_SECONDS", "12")))
+        s = reference_cpu_sample(spec, float(os.environ.get("CHOREO_CPU_BASELINE_SECONDS", "12")), host_cores())
         secs = run_reference_sample(s)
         cpu = {"value": s["units"] / secs / scale, "unit": unit, "cores": s["threads"],
                "kind": "reference" if s["use_ref"] else "port", "sample": sample_text(s, spec),
                "seconds": round(secs, 2)}
-    if exchange is not None:
-        case.info["exchanges_outside_timing"] = exchange
-    config = {"workload": spec["workload"], **case.info,
-              "l2": ("L2 flushed (256 MB written) between timed launches; per-launch events" if case.flush
-                     else "inputs larger than the 126 MB L2 (no flush needed)")}
+    if clocks is not None:
+        clocks["effective_sm_mhz"] = (1e3 * clk[0] / clk[1]) if clk[1] > 0 else None
+        clocks["effective_sm_mhz_how"] = (f"%clock64 / %globaltimer over the life of CTA 0 of each timed launch "
+                                          f"({clk[2]} launches, choreo_clock_probe_set)")
     line = {
         "metric": metric,
         "value": value,
@@ -659,18 +880,24 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
         "warmup": args.warmup,
         "ms_per_step": ms_max / args.steps,
         "higher_is_better": True,
-        "scaling": "strong" if world > 1 and (spec.get("m_total") == 65536 or spec["kind"] == "conv") else "weak",
+        "scaling": scaling_of(spec, world),
         "vs_baseline": None,
         "dtype": spec["dtype"],
         "data": "synthetic",
-        "config": config,
+        "config": config_block(spec, world),
+        "kernel": case.kernel,
         "roofline": roof,
         "e2e": {"value": e2e_value, "unit": unit, "h2d_bytes_per_step": case.h2d, "d2h_bytes_per_step": case.d2h,
-                "steps": e2e_steps, "ms_per_step": ms_e2e_max / e2e_steps},
+                "steps": e2e_steps, "ms_per_step": ms_e2e_max / e2e_steps,
+                "h2d_gbs_per_rank": case.h2d / (ms_e2e_max / e2e_steps * 1e-3) / 1e9, **case.e2e_info},
         "gpu_launches": args.steps * case.launches_per_step,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
+    if exchange is not None:
+        line["exchanges_outside_timing"] = exchange
+    if configs is not None:
+        line["configs"] = configs
     if unit == "TFLOP/s":
         line["pct_of_nominal_dense_peak"] = 100.0 * value / (NOMINAL_DENSE_TFLOPS * world)
     emit(line)
@@ -698,26 +925,25 @@ def main() -> None:
     os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="choreo", choices=["choreo", "reference"])
     ap.add_argument("--workload", default="auto",
-                    choices=["auto", "gemm8192", "sharded", "custom", "smallk", "conv", "relu"])
+                    choices=["auto", "sharded", "gemm8192", "custom", "smallk", "conv", "relu"])
     ap.add_argument("--shape", default=None, help="MxNxK for --workload custom")
     ap.add_argument("--dtype", default="f16", choices=["f16", "bf16"], help="input/output type for --workload custom")
     ap.add_argument("--tile", default=None,
                     help="force a kernel configuration: wide256, pair256, pair128, single256, single128 or single64")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the per-configuration block at N = 1")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    wl = args.workload if args.workload != "auto" else ("gemm8192" if world == 1 else "sharded")
-    spec = workload_spec(wl, world, args.shape, args.dtype)
-    if args.tile:
-        os.environ["CHOREO_GEMM_TILE"] = args.tile
+    wl = args.workload if args.workload != "auto" else "sharded"
+    spec = workload_spec(wl, args.shape, args.dtype)
 
     if args.impl == "reference":
         bench_reference(args, spec, world, rank)

@@ -85,6 +85,7 @@ _SIGNATURES = {
     "choreo_selftest_wait_timeout": (C.c_int, [C.c_double, C.c_void_p]),
     "choreo_tuning_set": (C.c_int, [C.POINTER(Tuning)]),
     "choreo_tuning_get": (C.c_int, [C.POINTER(Tuning)]),
+    "choreo_clock_probe_set": (C.c_int, [C.c_void_p]),
     "choreo_gemm_query": (C.c_int, [C.POINTER(GemmDesc), C.POINTER(LaunchConfig)]),
     "choreo_gemm": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p, C.c_size_t, C.c_void_p]),
     "choreo_gemm_noalloc": (C.c_int, [C.POINTER(GemmDesc), C.c_void_p]),
@@ -92,6 +93,15 @@ _SIGNATURES = {
                                          C.POINTER(C.c_void_p), C.POINTER(C.c_float)]),
     "choreo_shard_rows": (C.c_int, [C.c_int64, C.c_int, C.c_int, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
     "choreo_conv2d_query": (C.c_int, [C.POINTER(ConvDesc), C.POINTER(LaunchConfig)]),
+    "choreo_host_gemm_plan_create": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "choreo_host_conv_plan_create": (C.c_int, [C.POINTER(ConvDesc), C.c_int32, C.c_int32, C.POINTER(C.c_void_p)]),
+    "choreo_host_gemm_run": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32,
+                                       C.c_void_p]),
+    "choreo_host_conv_run": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32,
+                                       C.c_void_p]),
+    "choreo_host_plan_info_get": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "choreo_host_plan_part": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
+    "choreo_host_plan_destroy": (C.c_int, [C.c_void_p]),
     "choreo_conv2d": (C.c_int, [C.POINTER(ConvDesc), C.c_void_p, C.c_size_t, C.c_void_p]),
     "choreo_relu": (C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
     "choreo_add": (C.c_int, [C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
@@ -219,122 +229,124 @@ def gemm(a, b, c, *, trans_a=False, trans_b=False, alpha=1.0, beta=0.0, bias=Non
     gemm_desc(d, workspace, ws_bytes, stream)
 
 
-class HostGemmPlan:
-    """C = act(A @ B + bias) for row-major tensors in pinned HOST memory,
-    pipelined over the PCIe links: A is cut into row slabs (whole 512-row
-    tiles); the host->device copies of B, the bias and every slab of A run on
-    one copy stream, each slab's GEMM starts on the caller's stream as soon as
-    its rows have landed, and each slab of C goes back to the host on a second
-    copy stream as soon as it is computed. Device buffers and streams are
-    made once per plan and reused by every run(). run() returns with all of it
-    enqueued; the caller's stream is ordered after the last copy of C."""
+class HostGemmDesc(C.Structure):
+    _fields_ = [
+        ("m", C.c_int64), ("n", C.c_int64), ("k", C.c_int64),
+        ("dtype_ab", C.c_int32), ("dtype_c", C.c_int32), ("alpha", C.c_float),
+        ("has_bias", C.c_int32), ("dtype_bias", C.c_int32), ("relu", C.c_int32),
+        ("parts", C.c_int32), ("device", C.c_int32),
+    ]
 
-    def __init__(self, m, n, k, dtype, *, bias=False, relu=False, slabs=None, device=None):
-        import torch
-        self.m, self.n, self.k, self.relu = m, n, k, relu
-        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-        self.a = torch.empty(m, k, device=self.device, dtype=dtype)
-        self.b = torch.empty(k, n, device=self.device, dtype=dtype)
-        self.c = torch.empty(m, n, device=self.device, dtype=dtype)
-        self.bias = torch.empty(n, device=self.device, dtype=dtype) if bias else None
-        if slabs is None:  # ~1024-row slabs, at most 16: the last slab's GEMM and copy-out are the exposed tail
-            slabs = max(1, min(16, m // 1024))
-        per = -(-m // max(1, slabs))
-        per = max(512, -(-per // 512) * 512)
-        self.slabs = [(r0, min(per, m - r0)) for r0 in range(0, m, per)]
-        self.descs = [make_gemm_desc(self.a[r0:r0 + rows], self.b, self.c[r0:r0 + rows], m=rows, n=n, k=k,
-                                     bias=self.bias, relu=relu) for r0, rows in self.slabs]
-        qs = [gemm_query(d) for d in self.descs]
-        if any(q.workspace_min_bytes for q in qs):
-            raise ValueError("HostGemmPlan: operands must be TMA-legal (16-byte aligned rows)")
-        # One workspace (K-split partials) serves every slab: the slabs' GEMMs run in order on one stream.
-        self.ws_bytes = max(q.workspace_bytes for q in qs)
-        self.ws = torch.empty(max(1, self.ws_bytes), dtype=torch.uint8, device=self.device)
-        self.s_in = torch.cuda.Stream(self.device)
-        self.s_out = torch.cuda.Stream(self.device)
-        self.ev_in = [torch.cuda.Event() for _ in self.slabs]
-        self.ev_gemm = [torch.cuda.Event() for _ in self.slabs]
 
-    def run(self, a_h, b_h, c_h, bias_h=None, stream=None):
-        import torch
-        s = torch.cuda.current_stream(self.device) if stream is None else stream
-        self.s_in.wait_stream(s)    # the previous run's GEMMs have read the device buffers
-        self.s_out.wait_stream(s)
-        with torch.cuda.stream(self.s_in):
-            self.b.copy_(b_h, non_blocking=True)
-            if self.bias is not None:
-                self.bias.copy_(bias_h, non_blocking=True)
-            for (r0, rows), ev in zip(self.slabs, self.ev_in):
-                self.a[r0:r0 + rows].copy_(a_h[r0:r0 + rows], non_blocking=True)
-                ev.record(self.s_in)
-        for (r0, rows), d, ev_in, ev_g in zip(self.slabs, self.descs, self.ev_in, self.ev_gemm):
-            s.wait_event(ev_in)
-            gemm_desc(d, self.ws, self.ws_bytes, stream=s)
-            ev_g.record(s)
-            self.s_out.wait_event(ev_g)
-            with torch.cuda.stream(self.s_out):
-                c_h[r0:r0 + rows].copy_(self.c[r0:r0 + rows], non_blocking=True)
-        s.wait_stream(self.s_out)
+class HostPlanInfo(C.Structure):
+    _fields_ = [
+        ("parts", C.c_int32), ("launches_per_run", C.c_int32), ("device_bytes", C.c_int64),
+        ("h2d_bytes", C.c_int64), ("d2h_bytes", C.c_int64),
+    ]
+
+
+OPERANDS_ON_DEVICE = 1
+
+
+class _HostPlan:
+    """Owner of a choreo_host_plan (the C ABI's host-buffer pipeline)."""
+
+    def __init__(self, handle: C.c_void_p):
+        self._h = handle
+        self.info = HostPlanInfo()
+        check(lib.choreo_host_plan_info_get(self._h, C.byref(self.info)))
+        parts = []
+        for i in range(self.info.parts):
+            f, n = C.c_int64(), C.c_int64()
+            check(lib.choreo_host_plan_part(self._h, i, C.byref(f), C.byref(n)))
+            parts.append((f.value, n.value))
+        self.parts = parts
 
     def launches(self) -> int:
-        return len(self.slabs)
+        return self.info.launches_per_run
+
+    def close(self) -> None:
+        if self._h:
+            check(lib.choreo_host_plan_destroy(self._h))
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
-class HostConvPlan:
-    """conv2d for NHWC activations and KRSC weights in pinned HOST memory,
-    pipelined over the PCIe links like HostGemmPlan: the batch is cut into
-    runs of images; the weights, the bias and every run of activations go to
-    the device on one copy stream, each run's convolution starts on the
-    caller's stream as soon as its images have landed, and each run of output
-    goes back to the host on a second copy stream."""
+def _device_index(device) -> int:
+    import torch
+    if device is None:
+        return torch.cuda.current_device()
+    d = torch.device(device)
+    return d.index if d.index is not None else torch.cuda.current_device()
+
+
+class HostGemmPlan(_HostPlan):
+    """C = act(A @ B + bias) for row-major tensors in HOST memory through
+    choreo_host_gemm_run: A and C are cut into row slabs (whole 512-row
+    tiles); the copy of slab i+1 in, the GEMM of slab i and the copy of slab
+    i-1 out overlap on two library-owned copy streams and the caller's
+    stream. The plan owns its device buffers, made once by
+    choreo_host_gemm_plan_create. run() returns with everything enqueued; the
+    caller's stream is ordered after the last copy out. Pinned host tensors
+    get the overlap."""
+
+    def __init__(self, m, n, k, dtype, *, bias=False, relu=False, slabs=None, device=None, dtype_c=None):
+        import torch
+        code = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32}
+        d = HostGemmDesc()
+        d.m, d.n, d.k = m, n, k
+        d.dtype_ab = code[dtype]
+        d.dtype_c = code[dtype_c] if dtype_c is not None else d.dtype_ab
+        d.alpha = 1.0
+        d.has_bias, d.dtype_bias, d.relu = int(bool(bias)), d.dtype_ab, int(bool(relu))
+        d.parts = int(slabs or 0)
+        d.device = _device_index(device)
+        self.device = d.device
+        h = C.c_void_p()
+        check(lib.choreo_host_gemm_plan_create(C.byref(d), C.byref(h)))
+        super().__init__(h)
+        self.slabs = self.parts
+
+    def run(self, a_h, b, c_h, bias=None, stream=None, operands_on_device=False):
+        """a_h, c_h: host tensors; b, bias: host tensors, or device tensors of
+        the plan's device with operands_on_device=True."""
+        check(lib.choreo_host_gemm_run(self._h, _ptr(a_h), _ptr(b), _ptr(bias), _ptr(c_h),
+                                       OPERANDS_ON_DEVICE if operands_on_device else 0, _stream_ptr(stream)))
+
+
+class HostConvPlan(_HostPlan):
+    """conv2d for NHWC activations and KRSC weights in HOST memory through
+    choreo_host_conv_run: the batch is cut into runs of images, pipelined over
+    the PCIe links like HostGemmPlan."""
 
     def __init__(self, n, h, w, c, k, r, s, dtype, *, stride=1, padding=1, dilation=1, bias=False, relu=False,
                  runs=None, device=None):
         import torch
-        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-        p = (h + 2 * padding - dilation * (r - 1) - 1) // stride + 1
-        q = (w + 2 * padding - dilation * (s - 1) - 1) // stride + 1
-        self.x = torch.empty(n, h, w, c, device=self.device, dtype=dtype)
-        self.wt = torch.empty(k, r, s, c, device=self.device, dtype=dtype)
-        self.out = torch.empty(n, p, q, k, device=self.device, dtype=dtype)
-        self.bias = torch.empty(k, device=self.device, dtype=dtype) if bias else None
-        if runs is None:
-            runs = max(1, min(8, n // 2))
-        per = -(-n // max(1, runs))
-        self.runs = [(i0, min(per, n - i0)) for i0 in range(0, n, per)]
-        self.descs = [conv_desc(self.x[i0:i0 + cnt], self.wt, self.out[i0:i0 + cnt], stride=stride, padding=padding,
-                                dilation=dilation, bias=self.bias, relu=relu) for i0, cnt in self.runs]
-        for d in self.descs:
-            if conv2d_query(d).workspace_bytes:
-                raise ValueError("HostConvPlan: the convolution needs a workspace")
-        self.s_in = torch.cuda.Stream(self.device)
-        self.s_out = torch.cuda.Stream(self.device)
-        self.ev_in = [torch.cuda.Event() for _ in self.runs]
-        self.ev_conv = [torch.cuda.Event() for _ in self.runs]
+        code = {torch.float16: F16, torch.bfloat16: BF16}[dtype]
+        d = ConvDesc()
+        d.n, d.h, d.w, d.c, d.k, d.r, d.s = n, h, w, c, k, r, s
+        d.stride_h = d.stride_w = stride
+        d.pad_h = d.pad_w = padding
+        d.dil_h = d.dil_w = dilation
+        d.dtype = d.dtype_out = code
+        d.bias = 1 if bias else None  # non-NULL marks a plan with a bias; the pointer is not used
+        d.dtype_bias = code
+        d.relu = int(bool(relu))
+        d.alpha = 1.0
+        self.device = _device_index(device)
+        hdl = C.c_void_p()
+        check(lib.choreo_host_conv_plan_create(C.byref(d), int(runs or 0), self.device, C.byref(hdl)))
+        super().__init__(hdl)
+        self.runs = self.parts
 
-    def run(self, x_h, w_h, out_h, bias_h=None, stream=None):
-        import torch
-        st = torch.cuda.current_stream(self.device) if stream is None else stream
-        self.s_in.wait_stream(st)
-        self.s_out.wait_stream(st)
-        with torch.cuda.stream(self.s_in):
-            self.wt.copy_(w_h, non_blocking=True)
-            if self.bias is not None:
-                self.bias.copy_(bias_h, non_blocking=True)
-            for (i0, cnt), ev in zip(self.runs, self.ev_in):
-                self.x[i0:i0 + cnt].copy_(x_h[i0:i0 + cnt], non_blocking=True)
-                ev.record(self.s_in)
-        for (i0, cnt), d, ev_in, ev_c in zip(self.runs, self.descs, self.ev_in, self.ev_conv):
-            st.wait_event(ev_in)
-            conv2d_desc(d, stream=st)
-            ev_c.record(st)
-            self.s_out.wait_event(ev_c)
-            with torch.cuda.stream(self.s_out):
-                out_h[i0:i0 + cnt].copy_(self.out[i0:i0 + cnt], non_blocking=True)
-        st.wait_stream(self.s_out)
-
-    def launches(self) -> int:
-        return len(self.runs)
+    def run(self, x_h, w, out_h, bias=None, stream=None, operands_on_device=False):
+        check(lib.choreo_host_conv_run(self._h, _ptr(x_h), _ptr(w), _ptr(bias), _ptr(out_h),
+                                       OPERANDS_ON_DEVICE if operands_on_device else 0, _stream_ptr(stream)))
 
 
 def conv_desc(x, w, out, *, stride=1, padding=1, dilation=1, bias=None, relu=False, alpha=1.0) -> ConvDesc:

@@ -152,6 +152,12 @@ uint64_t wait_timeout_ns() {
 }
 
 namespace {
+thread_local unsigned long long* g_clock_probe = nullptr;
+}  // namespace
+
+unsigned long long* clock_probe() { return g_clock_probe; }
+
+namespace {
 void fill_device_cache(int dev) {
   DeviceCache& c = cache();
   std::lock_guard<std::mutex> lk(c.mu);
@@ -452,6 +458,17 @@ int choreo_tuning_set(const choreo_tuning* t) {
 int choreo_tuning_get(choreo_tuning* out) {
   if (out == nullptr) return fail(CHOREO_ERR_INVALID_ARG, "tuning: null output");
   *out = tuning().t;
+  return ok();
+}
+
+int choreo_clock_probe_set(void* probe) {
+  if (probe != nullptr) {
+    if (reinterpret_cast<uintptr_t>(probe) & 7u)
+      return fail(CHOREO_ERR_INVALID_ARG, "clock probe: the buffer must be 8-byte aligned");
+    int rc = check_device_ptr(probe, "clock probe");
+    if (rc) return rc;
+  }
+  g_clock_probe = static_cast<unsigned long long*>(probe);
   return ok();
 }
 

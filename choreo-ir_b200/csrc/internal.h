@@ -57,6 +57,8 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 uint32_t* status_word();
 // Per-wait time limit handed to kernels, in nanoseconds.
 uint64_t wait_timeout_ns();
+// This host thread's clock-probe buffer (choreo_clock_probe_set), or null.
+unsigned long long* clock_probe();
 // SM count and opt-in shared memory of the current device (cached).
 int current_sm_count();
 int current_smem_optin();

@@ -67,7 +67,27 @@ struct TcParams {
   // failure reporting
   uint32_t* status;
   uint64_t timeout_ns;
+  // measurement hook (null = off): CTA 0 adds the SM clock cycles and the
+  // %globaltimer nanoseconds of its lifetime to [0] and [1], and 1 to [2]
+  unsigned long long* clock_probe;
 };
+
+// Start / end stamps of the clock probe, kept in the CTA's barrier block.
+__device__ __forceinline__ void probe_start(const TcParams& p, uint64_t* slot) {
+  if (p.clock_probe != nullptr && blockIdx.x == 0) {
+    slot[0] = static_cast<uint64_t>(clock64());
+    slot[1] = globaltimer_ns();
+  }
+}
+__device__ __forceinline__ void probe_end(const TcParams& p, const uint64_t* slot) {
+  if (p.clock_probe != nullptr && blockIdx.x == 0 && threadIdx.x == 0) {
+    const uint64_t ns = globaltimer_ns();
+    const uint64_t clk = static_cast<uint64_t>(clock64());
+    atomicAdd(p.clock_probe, static_cast<unsigned long long>(clk - slot[0]));
+    atomicAdd(p.clock_probe + 1, static_cast<unsigned long long>(ns - slot[1]));
+    atomicAdd(p.clock_probe + 2, 1ull);
+  }
+}
 
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
@@ -337,6 +357,7 @@ struct alignas(8) TcBarriers {
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];
   uint64_t drain;
+  uint64_t probe[2];
   uint32_t tmem_base;
   int32_t abort;
 };
@@ -387,6 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.c_tma) tma_prefetch_desc(&tma_c);
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort = 0;
+    probe_start(p, bars->probe);
     fence_mbar_init();
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
@@ -512,6 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  probe_end(p, bars->probe);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
@@ -576,6 +599,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (p.c_tma) tma_prefetch_desc(&tma_c);
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort = 0;
+    probe_start(p, bars->probe);
     fence_mbar_init();
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
@@ -719,6 +743,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   cluster_sync();  // both CTAs done (MMAs drained, epilogues finished) before TMEM is freed
+  probe_end(p, bars->probe);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols);
@@ -746,6 +771,7 @@ struct alignas(8) TcWideBarriers {
   uint64_t tmem_full[2];   // accumulator half h of this tile is complete (leader commit, count 1)
   uint64_t tmem_empty[2];  // accumulator half h read out by the pair's 16 epilogue warps (leader's, count 16)
   uint64_t drain;
+  uint64_t probe[2];
   uint32_t tmem_base;
   int32_t abort;
 };
@@ -796,6 +822,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(smem_u32(&bars->tmem_empty[1]), 2 * kEpiWarps);
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort = 0;
+    probe_start(p, bars->probe);
     fence_mbar_init();
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
@@ -1007,6 +1034,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   cluster_sync();
+  probe_end(p, bars->probe);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols);

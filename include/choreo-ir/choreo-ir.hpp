@@ -21,6 +21,7 @@
 #include "compute/compute.hpp"
 #include "compute/conv.hpp"
 #include "compute/elementwise.hpp"
+#include "compute/host_pipeline.hpp"
 #include "compute/matmul.hpp"
 #include "compute/validation.hpp"
 #include "core/config.hpp"

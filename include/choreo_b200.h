@@ -177,6 +177,17 @@ int choreo_tuning_set(const choreo_tuning* t);
 /* Copies the settings in force into *out. */
 int choreo_tuning_get(choreo_tuning* out);
 
+/* Measurement hook: while `probe` is set (non-NULL) on this host thread,
+ * every tensor-core GEMM and conv launched from the thread adds, from its
+ * first CTA, the SM clock cycles (%clock64) and the global-timer nanoseconds
+ * (%globaltimer) between that CTA's start and its end to probe[0] and
+ * probe[1], and 1 to probe[2]: probe[0] / probe[1] is the effective SM clock
+ * in GHz during those kernels. `probe` is three 8-byte-aligned uint64 in
+ * device memory of the device the kernels run on, zeroed by the caller.
+ * NULL turns it off. Reads clocks only; changes no setting. No counterpart in
+ * the reference (its utils/profiler.hpp times with CUDA events only). */
+int choreo_clock_probe_set(void* probe);
+
 /* Launches one CTA that waits, through the bounded wait every kernel
  * pipeline uses, on an mbarrier nothing arrives on. The wait gives up after
  * timeout_ms, records a timeout in the status word and the kernel returns:
@@ -253,6 +264,77 @@ int choreo_conv2d_query(const choreo_conv_desc* d, choreo_launch_config* out);
  * with the semantics of benchmark/kernels/gemm_example.cu:208-253, in NHWC. */
 int choreo_conv2d(const choreo_conv_desc* d, void* workspace, size_t workspace_bytes,
                   void* stream);
+
+/* ---- host-buffer pipelines ----------------------------------------------
+ * The reference moves data with Tensor::to_device()/to_host() (synchronous
+ * cudaMemcpy, tensor/tensor.hpp:568-598, README.md:86-94) around a device
+ * operator*. A host plan does the same job for inputs and outputs that live
+ * in host memory, with the copies overlapped with the kernels: A (GEMM) or
+ * the image batch (conv) is cut into parts; the host->device copy of part
+ * i+1, the kernel of part i and the device->host copy of part i-1 run at
+ * the same time on two library-owned copy streams and the caller's stream.
+ * The plan owns its device buffers (allocated once, at create), its copy
+ * streams and events; run() allocates nothing. Host memory that is pinned
+ * (cudaHostAlloc / cudaHostRegister) gets the overlap; pageable memory works
+ * but the driver stages its copies. A plan is used by one host thread at a
+ * time; run() is asynchronous on `stream` like every other call: the host
+ * buffers must stay valid and unchanged until the stream reaches the end of
+ * the run. */
+typedef struct choreo_host_plan choreo_host_plan;   /* opaque */
+
+/* B and bias (GEMM), weight and bias (conv) are device memory of the plan's
+ * device, read in place instead of copied from the host. */
+#define CHOREO_HOST_OPERANDS_ON_DEVICE 1
+
+/* C = act(alpha * A B + bias) for row-major contiguous A [m x k], B [k x n],
+ * C [m x n] (leading dimensions k, n, n) and an optional n-vector bias. */
+typedef struct choreo_host_gemm_desc {
+  int64_t m, n, k;
+  int32_t dtype_ab, dtype_c;   /* as choreo_gemm_desc */
+  float alpha;
+  int32_t has_bias, dtype_bias;
+  int32_t relu;
+  int32_t parts;               /* row slabs of A and C; 0 = library choice (~1024-row slabs, at most 16) */
+  int32_t device;              /* CUDA device the plan runs on */
+} choreo_host_gemm_desc;
+
+typedef struct choreo_host_plan_info {
+  int32_t parts;               /* row slabs (GEMM) or image runs (conv) */
+  int32_t launches_per_run;    /* kernels one run enqueues */
+  int64_t device_bytes;        /* device memory the plan holds */
+  int64_t h2d_bytes;           /* bytes one run copies in (operands from the host) */
+  int64_t d2h_bytes;           /* bytes one run copies out */
+} choreo_host_plan_info;
+
+/* Makes a GEMM plan: validates *d, allocates the device buffers, the copy
+ * streams and events on d->device. */
+int choreo_host_gemm_plan_create(const choreo_host_gemm_desc* d, choreo_host_plan** out);
+
+/* Makes a conv plan for the shape in *d: its data pointers are not used,
+ * except that a non-NULL d->bias makes a plan with a bias; alpha, bias type
+ * and ReLU are taken from it. The batch is cut into `parts` runs of images
+ * (0 = library choice, at most 8). */
+int choreo_host_conv_plan_create(const choreo_conv_desc* d, int32_t parts, int32_t device,
+                                 choreo_host_plan** out);
+
+/* One GEMM through a GEMM plan: a and c in host memory; b and bias (NULL when
+ * the plan has none) in host memory, or on the plan's device with
+ * CHOREO_HOST_OPERANDS_ON_DEVICE in flags. */
+int choreo_host_gemm_run(choreo_host_plan* p, const void* a, const void* b, const void* bias, void* c,
+                         int32_t flags, void* stream);
+
+/* One convolution through a conv plan (input NHWC and output in host memory;
+ * weight KRSC and bias as b and bias above). */
+int choreo_host_conv_run(choreo_host_plan* p, const void* input, const void* weight, const void* bias,
+                         void* output, int32_t flags, void* stream);
+
+int choreo_host_plan_info_get(const choreo_host_plan* p, choreo_host_plan_info* out);
+
+/* Part i of the plan: first row (GEMM) or image (conv) and count. */
+int choreo_host_plan_part(const choreo_host_plan* p, int32_t i, int64_t* first, int64_t* count);
+
+/* Waits for the plan's work, frees its device buffers, streams and events. */
+int choreo_host_plan_destroy(choreo_host_plan* p);
 
 /* ---- elementwise (device kernels replacing host round trips) ---------- */
 

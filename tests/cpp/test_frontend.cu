@@ -478,6 +478,53 @@ TEST(gpu_conv, Conv2dAgainstFp64) {
   EXPECT_LE(worst, 1e-2);
 }
 
+TEST(gpu_host_pipeline, GemmAndConvOnHostTensors) {
+  initialize();
+  // GEMM: host A, B, bias -> host C through the pipelined host plan, with the
+  // host buffers page-locked for the run; then B and bias resident on the device.
+  auto A = host_tensor<bfloat16_t>::random({1100, 256}, -1, 1, 71);
+  auto B = host_tensor<bfloat16_t>::random({256, 192}, -1, 1, 72);
+  auto bias = host_tensor<bfloat16_t>::random({192}, -0.5f, 0.5f, 73);
+  auto C = host_tensor<bfloat16_t>::zeros({1100, 192});
+  {
+    PinnedHost pa(A), pc(C);
+    compute::HostGemmPlan<bfloat16_t> plan(1100, 192, 256, /*has_bias=*/true, /*relu=*/true, /*parts=*/3);
+    EXPECT_EQ(plan.info().parts, 3);  // 367-row parts rounded up to 512-row tiles: 512, 512, 76
+    plan.run(A, B, C, &bias);
+    plan.synchronize();
+    auto C2 = host_tensor<bfloat16_t>::zeros({1100, 192});
+    auto Bd = B.to_device();
+    auto biasd = bias.to_device();
+    plan.run(A, Bd, C2, &biasd);
+    plan.synchronize();
+    for (index_t i = 0; i < C.numel(); ++i) EXPECT_EQ(to_float(C.data()[i]), to_float(C2.data()[i]));
+  }
+  double worst = 0, ss = 0;
+  std::vector<double> r(1100 * 192);
+  for (int i = 0; i < 1100; ++i)
+    for (int j = 0; j < 192; ++j) {
+      double s = to_float(bias(j));
+      for (int k = 0; k < 256; ++k) s += double(to_float(A(i, k))) * double(to_float(B(k, j)));
+      r[i * 192 + j] = s < 0 ? 0 : s;
+      ss += s * s;
+    }
+  const double tau = 1e-3 * std::sqrt(ss / r.size());
+  for (size_t i = 0; i < r.size(); ++i)
+    worst = std::max(worst, std::fabs(to_float(C.data()[i]) - r[i]) / std::max(std::fabs(r[i]), tau));
+  EXPECT_LE(worst, 1e-2);
+  // conv: host activations and weights -> host output; equals the device conv2d.
+  auto in = host_tensor<half>::random({3, 8, 9, 64}, 0, 1, 74);
+  auto w = host_tensor<half>::random({64, 3, 3, 64}, -0.05f, 0.05f, 75);
+  compute::HostConvPlan<half> cplan(in.shape(), w.shape(), 1, 1, false, false, 2);
+  auto out = host_tensor<half>::zeros(cplan.output_shape());
+  cplan.run(in, w, out);
+  cplan.synchronize();
+  auto ref = conv2d(in.to_device(), w.to_device(), 1, 1).to_host();
+  for (index_t i = 0; i < out.numel(); ++i) EXPECT_EQ(to_float(out.data()[i]), to_float(ref.data()[i]));
+  // contract: a device tensor where the plan streams host memory
+  EXPECT_THROW(cplan.run(in.to_device(), w, out), std::runtime_error);
+}
+
 namespace {
 __global__ void fill_grid_kernel(int* out, int value) {
   if (threadIdx.x == 0) out[blockIdx.x] = value;

@@ -49,6 +49,8 @@ def test_struct_layout_matches_c_compiler(cb, tmp_path):
         "choreo_conv_desc": cb.ConvDesc,
         "choreo_device_props": cb.DeviceProps,
         "choreo_tuning": cb.Tuning,
+        "choreo_host_gemm_desc": cb.HostGemmDesc,
+        "choreo_host_plan_info": cb.HostPlanInfo,
     }
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void) {"]
     for cname, py in structs.items():
@@ -243,3 +245,29 @@ def test_library_reads_no_environment():
     nothing."""
     for f in (ROOT / "choreo-ir_b200" / "csrc").glob("*.cu*"):
         assert "getenv" not in f.read_text(), f.name
+
+
+# ------------------------------------------------------------------ host-buffer plans: contracts checked before any CUDA call
+def test_host_plan_contract_errors(cb):
+    d = cb.HostGemmDesc()
+    d.m, d.n, d.k, d.dtype_ab, d.dtype_c = 0, 64, 64, cb.F16, cb.F16
+    h = C.c_void_p()
+    assert cb.lib.choreo_host_gemm_plan_create(C.byref(d), C.byref(h)) == -1
+    assert "Invalid matrix dimensions" in cb.lib.choreo_last_error().decode() and not h.value
+    d.m, d.dtype_ab = 64, 3
+    assert cb.lib.choreo_host_gemm_plan_create(C.byref(d), C.byref(h)) == -2
+    d.dtype_ab, d.k = cb.F16, 12  # 24-byte rows of A: not TMA-addressable
+    assert cb.lib.choreo_host_gemm_plan_create(C.byref(d), C.byref(h)) == -2
+    assert "multiple of 16 bytes" in cb.lib.choreo_last_error().decode()
+    d.k, d.parts = 64, -1
+    assert cb.lib.choreo_host_gemm_plan_create(C.byref(d), C.byref(h)) == -1
+    assert cb.lib.choreo_host_gemm_plan_create(None, C.byref(h)) == -1
+    cd = cb.ConvDesc()
+    cd.n, cd.h, cd.w, cd.c, cd.k, cd.r, cd.s = 2, 8, 8, 16, 16, 3, 3
+    cd.stride_h = cd.stride_w = cd.dil_h = cd.dil_w = 0
+    assert cb.lib.choreo_host_conv_plan_create(C.byref(cd), 0, 0, C.byref(h)) == -1
+    # runs and queries on something that is not a plan of that kind
+    assert cb.lib.choreo_host_gemm_run(None, 0x1000, 0x2000, None, 0x3000, 0, None) == -1
+    assert cb.lib.choreo_host_conv_run(None, 0x1000, 0x2000, None, 0x3000, 0, None) == -1
+    assert cb.lib.choreo_host_plan_info_get(None, None) == -1
+    assert cb.lib.choreo_host_plan_destroy(None) == 0

@@ -1,0 +1,126 @@
+"""Host-buffer pipelines (choreo_host_gemm_* / choreo_host_conv_*) on the GPU,
+driven through the C ABI with raw pointers (ctypes), checked against the CPU
+oracle.
+
+These stand behind the reference's to_device() -> operator* -> to_host() flow
+(tensor/tensor.hpp:568-598): inputs and outputs in host memory, the copies
+overlapped with the kernels by the library. Cases: pinned and pageable host
+memory, B (or the weights) already resident on the device, two runs queued
+back to back on one plan without a synchronize between them, a ragged last
+part, and the run-time contract errors.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from _util import BF16, F16, as_f64, assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _bits(t):
+    import torch
+    return t.view(torch.int16).numpy().view(np.uint16)
+
+
+def _gemm_plan(cb, m, n, k, dt, *, bias, relu, parts=0):
+    d = cb.HostGemmDesc()
+    d.m, d.n, d.k = m, n, k
+    d.dtype_ab = d.dtype_c = d.dtype_bias = dt
+    d.alpha = 1.0
+    d.has_bias, d.relu, d.parts, d.device = int(bias), int(relu), parts, 0
+    h = C.c_void_p()
+    cb.check(cb.lib.choreo_host_gemm_plan_create(C.byref(d), C.byref(h)))
+    return h
+
+
+def test_host_gemm_run_through_c_abi_pinned(cb, cuda, orc):
+    """Raw C ABI: create, query parts and info, two runs enqueued back to back
+    (new inputs each, no synchronize between them), destroy."""
+    import torch
+    m, n, k = 2100, 640, 384
+    h = _gemm_plan(cb, m, n, k, BF16, bias=True, relu=True, parts=4)
+    info = cb.HostPlanInfo()
+    cb.check(cb.lib.choreo_host_plan_info_get(h, C.byref(info)))
+    # 4 parts asked: 525 rows each, rounded up to whole 512-row tiles -> 3 parts
+    assert info.parts == 3 and info.launches_per_run >= 3
+    assert info.h2d_bytes == 2 * (m * k + k * n + n) and info.d2h_bytes == 2 * m * n
+    assert info.device_bytes >= 2 * (m * k + k * n + m * n)
+    spans = []
+    for i in range(info.parts):
+        f, c = C.c_int64(), C.c_int64()
+        cb.check(cb.lib.choreo_host_plan_part(h, i, C.byref(f), C.byref(c)))
+        spans.append((f.value, c.value))
+    assert spans == [(0, 1024), (1024, 1024), (2048, 52)]
+    runs = []
+    stream = torch.cuda.current_stream().cuda_stream
+    for seed in (11, 21):
+        g = torch.Generator().manual_seed(seed)
+        a = torch.empty(m, k).uniform_(-1, 1, generator=g).bfloat16().pin_memory()
+        b = torch.empty(k, n).uniform_(-1, 1, generator=g).bfloat16().pin_memory()
+        bias = torch.empty(n).normal_(0, 0.3, generator=g).bfloat16().pin_memory()
+        c = torch.full((m, n), 5.0, dtype=torch.bfloat16).pin_memory()
+        cb.check(cb.lib.choreo_host_gemm_run(h, a.data_ptr(), b.data_ptr(), bias.data_ptr(), c.data_ptr(), 0, stream))
+        runs.append((a, b, bias, c))
+    torch.cuda.current_stream().synchronize()
+    cb.sync_status()
+    cb.check(cb.lib.choreo_host_plan_destroy(h))
+    for a, b, bias, c in runs:
+        r = orc.gemm_f64(_bits(a), _bits(b), BF16, bias=_bits(bias), dtype_bias=BF16, relu=True)
+        assert_close(as_f64(_bits(c), BF16), r, what="host GEMM plan", k=k)
+
+
+def test_host_gemm_operands_on_device_and_pageable(cb, cuda, orc):
+    """B and bias already on the device (CHOREO_HOST_OPERANDS_ON_DEVICE), A and
+    C in pageable (numpy) host memory."""
+    import torch
+    m, n, k = 1030, 256, 512
+    h = _gemm_plan(cb, m, n, k, F16, bias=True, relu=False)
+    a = orc.to_bits(orc.uniform((m, k), -1, 1, 61), F16)
+    b = orc.to_bits(orc.uniform((k, n), -1, 1, 62), F16)
+    bias = orc.to_bits(orc.normal((n,), 0, 0.2, 63), F16)
+    bd = torch.from_numpy(b.view(np.int16)).cuda()
+    biasd = torch.from_numpy(bias.view(np.int16)).cuda()
+    c = np.zeros((m, n), np.uint16)
+    stream = torch.cuda.current_stream().cuda_stream
+    cb.check(cb.lib.choreo_host_gemm_run(h, a.ctypes.data, bd.data_ptr(), biasd.data_ptr(), c.ctypes.data,
+                                         cb.OPERANDS_ON_DEVICE, stream))
+    torch.cuda.current_stream().synchronize()
+    cb.sync_status()
+    r = orc.gemm_f64(a, b, F16, bias=bias, dtype_bias=F16)
+    assert_close(as_f64(c, F16), r, what="host GEMM plan, B on device", k=k)
+    # contract errors at run time: device memory where host memory belongs,
+    # host memory where the flag promises device memory, a missing bias
+    assert cb.lib.choreo_host_gemm_run(h, bd.data_ptr(), bd.data_ptr(), biasd.data_ptr(), c.ctypes.data, 0,
+                                       stream) == cb.ERR_INVALID_ARG
+    assert cb.lib.choreo_host_gemm_run(h, a.ctypes.data, b.ctypes.data, biasd.data_ptr(), c.ctypes.data,
+                                       cb.OPERANDS_ON_DEVICE, stream) == cb.ERR_INVALID_ARG
+    assert cb.lib.choreo_host_gemm_run(h, a.ctypes.data, b.ctypes.data, None, c.ctypes.data, 0,
+                                       stream) == cb.ERR_INVALID_ARG
+    assert "with a bias" in cb.lib.choreo_last_error().decode()
+    cb.check(cb.lib.choreo_host_plan_destroy(h))
+
+
+def test_host_conv_weights_on_device(cb, cuda, orc):
+    """HostConvPlan with the weights and bias resident on the device, a
+    ragged last run of images, against fp64."""
+    import torch
+    n, hh, ww, c, k = 5, 9, 11, 64, 128
+    plan = cb.HostConvPlan(n, hh, ww, c, k, 3, 3, torch.float16, bias=True, relu=True, runs=3)
+    assert [cnt for _, cnt in plan.runs] == [2, 2, 1]
+    x = orc.to_bits(orc.uniform((n, hh, ww, c), 0, 1, 91), F16)
+    wt = orc.to_bits(orc.normal((k, 3, 3, c), 0, 1.0 / 24, 92), F16)
+    bias = orc.to_bits(orc.normal((k,), 0, 0.1, 93), F16)
+    xh = torch.from_numpy(x.view(np.int16)).view(torch.float16).pin_memory()
+    wd = torch.from_numpy(wt.view(np.int16)).view(torch.float16).cuda()
+    bd = torch.from_numpy(bias.view(np.int16)).view(torch.float16).cuda()
+    out = torch.zeros(n, hh, ww, k, dtype=torch.float16).pin_memory()
+    plan.run(xh, wd, out, bd, operands_on_device=True)
+    torch.cuda.current_stream().synchronize()
+    cb.sync_status()
+    ref = orc.conv2d_f64(x, wt, F16, bias=bias, dtype_bias=F16, relu=True)
+    assert_close(as_f64(_bits(out), F16).reshape(-1, k), ref, what="host conv plan, weights on device", k=9 * c)
+    plan.close()

@@ -126,9 +126,9 @@ def test_failed_rank_is_detected_not_hung(tmp_path):
 def test_bench_workload_specs():
     sys.path.insert(0, str(ROOT))
     import bench
-    s = bench.workload_spec("sharded", 8)
+    s = bench.workload_spec("sharded")
     assert (s["m_total"], s["n"], s["k"], s["dtype"], s["bias"], s["relu"]) == (65536, 8192, 8192, "bf16", True, True)
-    g = bench.workload_spec("gemm8192", 1)
+    g = bench.workload_spec("gemm8192")
     assert (g["m_total"], g["n"], g["k"], g["dtype"]) == (8192, 8192, 8192, "f16")
 
 
@@ -142,3 +142,43 @@ def test_bench_conv_batch_split():
         assert sum(c for _, c in runs) == 32
         assert all(runs[i][0] + runs[i][1] == runs[i + 1][0] for i in range(world - 1))
         assert max(c for _, c in runs) - min(c for _, c in runs) <= 1
+
+
+def test_bench_shard_rows_matches_library(cb):
+    """bench.py's restated partition (used by the reference arm, which loads no
+    GPU library) is choreo_shard_rows's."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    for m in (1, 127, 4097, 65536, 65536 + 5):
+        for world in (1, 2, 3, 4, 8):
+            for r in range(world):
+                assert bench.shard_rows(m, world, r) == cb.shard_rows(m, world, r)
+
+
+def test_bench_reference_arm_line(tmp_path):
+    """The reference arm on the CPU: one JSON line whose `config` is exactly the
+    block the GPU arm prints for the same workload and GPU count (the default
+    workload, the row-sharded GEMM, at every N), and whose core count is the
+    host's, not torchrun's OMP_NUM_THREADS=1."""
+    import json
+    import os
+    import subprocess
+    sys.path.insert(0, str(ROOT))
+    import bench
+    env = dict(os.environ, CHOREO_REF_STEP_SECONDS="0.05", OMP_NUM_THREADS="1", WORLD_SIZE="2", RANK="0")
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "3"],
+                       capture_output=True, text=True, env=env, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["n_gpus"] == 2
+    assert line["config"] == bench.config_block(bench.workload_spec("sharded"), 2)
+    assert line["config"]["workload"] == "rowsharded_gemm_bf16_65536x8192x8192_bias_relu"
+    assert line["cpu_baseline"]["cores"] == bench.host_cores()
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["metric"] == bench.HEADLINE_METRIC
+    # rank 1 of the same run does no work and prints nothing
+    env["RANK"] = "1"
+    r1 = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1"],
+                        capture_output=True, text=True, env=env, timeout=120)
+    assert r1.returncode == 0 and r1.stdout.strip() == ""
