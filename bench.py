@@ -89,10 +89,11 @@ def _gemm(workload, m, n, k, dtype, dist, bias, relu, layout="NN"):
                 relu=relu, layout=layout)
 
 
-def workload_spec(name: str, shape: str | None = None, dtype: str = "f16") -> dict:
+def workload_spec(name: str, shape: str | None = None, dtype: str = "f16", layout: str = "NN") -> dict:
     if name == "custom":
         m, n, k = (int(x) for x in (shape or "4096x4096x4096").lower().split("x"))
-        return _gemm(f"gemm_{dtype}_{m}x{n}x{k}", m, n, k, dtype, "U[-1,1]", False, False)
+        suffix = "" if layout == "NN" else f"_{layout}"
+        return _gemm(f"gemm_{dtype}_{m}x{n}x{k}{suffix}", m, n, k, dtype, "U[-1,1]", False, False, layout)
     if name == "gemm8192":
         return _gemm("gemm_f16_8192x8192x8192", 8192, 8192, 8192, "f16", "U[-1,1]", False, False)
     if name == "sharded":
@@ -469,20 +470,31 @@ def setup_gemm(cb, spec, world, rank, dev, stream) -> Case:
     r0, rows = cb.shard_rows(M_total, world, rank)
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
-    a = torch.empty(rows, K, device=dev).uniform_(lo, hi, generator=g).to(dt)
+    ta, tb = spec["layout"][0] == "T", spec["layout"][1] == "T"   # A stored K x M / B stored N x K
+    a = torch.empty((K, rows) if ta else (rows, K), device=dev).uniform_(lo, hi, generator=g).to(dt)
     g.manual_seed(99)  # B and bias are replicas: same seed on every rank
-    b = torch.empty(K, N, device=dev).uniform_(lo, hi, generator=g).to(dt)
+    b = torch.empty((N, K) if tb else (K, N), device=dev).uniform_(lo, hi, generator=g).to(dt)
     bias = torch.empty(N, device=dev).normal_(0.0, 0.1, generator=g).to(dt) if spec["bias"] else None
     c = torch.empty(rows, N, device=dev, dtype=dt)
-    desc = cb.make_gemm_desc(a, b, c, m=rows, n=N, k=K, bias=bias, relu=spec["relu"])
+    desc = cb.make_gemm_desc(a, b, c, m=rows, n=N, k=K, trans_a=ta, trans_b=tb, lda=a.stride(0), ldb=b.stride(0),
+                             bias=bias, relu=spec["relu"])
     q = cb.gemm_query(desc)
     case = Case()
-    # Row-major operands with 16-byte rows never need a repack; a workspace is
-    # only the fp32 partials of a K split (few output tiles over a long K).
-    assert q.workspace_min_bytes == 0
+    # The workspace holds the repack of an operand whose rows are not 16-byte
+    # aligned (each one a launch before the GEMM) and the fp32 partials of a
+    # K split (plus its reduction pass).
     ws = torch.empty(max(1, q.workspace_bytes), dtype=torch.uint8, device=dev)
     case.step = lambda: cb.gemm_desc(desc, ws, q.workspace_bytes, stream=stream)
-    case.launches_per_step = 2 if q.split_k > 1 else 1  # the split's reduction pass
+    repacks = int(a.stride(0) * 2 % 16 != 0) + int(b.stride(0) * 2 % 16 != 0)
+    case.launches_per_step = 1 + repacks + (1 if q.split_k > 1 else 0)
+    if spec["layout"] != "NN":
+        # the host-buffer plans stream row-major NN operands only
+        case.rows = rows
+        case.flops, case.bytes_ = spec_flops_bytes(spec, rows)
+        case.units_total = spec_flops_bytes(spec)[0]
+        case.flush = flushes_l2(spec, world)
+        case.kernel = {"name": kernel_name(q), "tile": f"{q.tile_m}x{q.tile_n}x{q.tile_k}", "repacks": repacks}
+        return case
     a_h, b_h = _pinned_copy(a), _pinned_copy(b)
     bias_h = _pinned_copy(bias) if bias is not None else None
     c_h = torch.empty(rows, N, dtype=dt, pin_memory=True)
@@ -640,34 +652,66 @@ class Flusher:
         self.buf.fill_(1.0)
 
 
-def median_launch_ms(fn, stream, flush, reps: int, warmup: int = 3) -> float:
-    """Median device time of one call of fn, each call bracketed by its own
-    events on `stream`, the L2 overwritten between calls (outside the events)."""
+def ab_timing(cb, ours, ref, stream, flush, reps: int, probe, warmup: int = 3) -> dict:
+    """Our launch and the side reference's, timed alternately so both see the
+    same clocks and power state:
+      flushed: median device time of one call, each call bracketed by its own
+               events on `stream`, the L2 overwritten before every call
+               (outside the events) - the timing rule of the headline;
+      back_to_back: mean over `reps` calls issued back to back (warm L2; our
+               launches overlap their prologue with the previous one's tail);
+      effective_sm_mhz: SM clock during our flushed calls, from the in-kernel
+               probe (%clock64 / %globaltimer of CTA 0)."""
     import torch
     for _ in range(warmup):
-        fn()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-    for s, e in evs:
+        ours()
+        ref()
+    probe.zero_()
+    cb.check(cb.lib.choreo_clock_probe_set(probe.data_ptr()))
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    mine = [(ev(), ev()) for _ in range(reps)]
+    theirs = [(ev(), ev()) for _ in range(reps)]
+    for (a0, a1), (b0, b1) in zip(mine, theirs):
         flush()
-        s.record(stream)
-        fn()
-        e.record(stream)
-    evs[-1][1].synchronize()
-    return statistics.median(s.elapsed_time(e) for s, e in evs)
+        a0.record(stream)
+        ours()
+        a1.record(stream)
+        flush()
+        b0.record(stream)
+        ref()
+        b1.record(stream)
+    theirs[-1][1].synchronize()
+    cb.check(cb.lib.choreo_clock_probe_set(None))
+    clk = [int(v) for v in probe.cpu()]
+    flushed = statistics.median(a.elapsed_time(b) for a, b in mine)
+    flushed_ref = statistics.median(a.elapsed_time(b) for a, b in theirs)
+    b2b = []
+    for fn in (ours, ref):
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        b2b.append(e0.elapsed_time(e1) / reps)
+    return {"ms": flushed, "ms_ref": flushed_ref, "ms_b2b": b2b[0], "ms_ref_b2b": b2b[1],
+            "mhz": (1e3 * clk[0] / clk[1]) if clk[1] else None}
 
 
 def run_configs(cb, dev, stream, reps: int) -> list[dict]:
     """The other configurations of the benchmark suite on this GPU, each timed
-    through the C ABI as the median of `reps` L2-flushed launches, next to
-    cuBLAS / cuDNN (through torch) on the same inputs as a side reference."""
+    through the C ABI as the median of `reps` L2-flushed launches, alternating
+    with cuBLAS / cuDNN (through torch) on the same inputs as a side
+    reference; back-to-back means and the effective SM clock beside them."""
     import torch
     import torch.nn.functional as Fn
     peak, peak_src = measured_peak(0.0)
     hbm, _ = measured_hbm()
     flush = Flusher(dev)
+    probe = torch.zeros(3, dtype=torch.int64, device=dev)
     out = []
 
-    def gemm_entry(name, cfg, m, n, k, dt, layout, dist):
+    def gemm_entry(cfg, m, n, k, dt, layout, dist):
         g = torch.Generator(device=dev)
         g.manual_seed(m + 3 * n + 7 * k)
         tdt = torch.float16 if dt == "f16" else torch.bfloat16
@@ -683,11 +727,12 @@ def run_configs(cb, dev, stream, reps: int) -> list[dict]:
         d = cb.make_gemm_desc(a, b, c, m=m, n=n, k=k, trans_a=ta, trans_b=tb, lda=a.stride(0), ldb=b.stride(0))
         q = cb.gemm_query(d)
         ws = torch.empty(max(1, q.workspace_bytes), dtype=torch.uint8, device=dev)
-        ms = median_launch_ms(lambda: cb.gemm_desc(d, ws, q.workspace_bytes, stream=stream), stream, flush, reps)
-        cb.sync_status(stream)
         opa = a.t() if ta else a
         opb = b.t() if tb else b
-        ms_ref = median_launch_ms(lambda: torch.matmul(opa, opb), stream, flush, reps)
+        t = ab_timing(cb, lambda: cb.gemm_desc(d, ws, q.workspace_bytes, stream=stream), lambda: torch.matmul(opa, opb),
+                      stream, flush, reps, probe)
+        cb.sync_status(stream)
+        ms, ms_ref = t["ms"], t["ms_ref"]
         flops = 2.0 * m * n * k
         byts = 2.0 * (m * k + k * n + m * n)
         tf = flops / (ms * 1e-3) / 1e12
@@ -697,9 +742,12 @@ def run_configs(cb, dev, stream, reps: int) -> list[dict]:
              "us": round(ms * 1e3, 2), "tflops": round(tf, 1), "gbs": round(byts / (ms * 1e-3) / 1e9, 1),
              "bound": bound,
              "frac": round(tf / peak, 4) if bound == "tensor" else round(byts / (ms * 1e-3) / 1e9 / hbm, 4),
+             "us_back_to_back": round(t["ms_b2b"] * 1e3, 2), "effective_sm_mhz": t["mhz"] and round(t["mhz"]),
              "side_reference": {"what": "cuBLAS via torch.matmul, same inputs and layout", "us": round(ms_ref * 1e3, 2),
-                                "tflops": round(flops / (ms_ref * 1e-3) / 1e12, 1)},
-             "time_vs_side_reference": round(ms / ms_ref, 3)}
+                                "tflops": round(flops / (ms_ref * 1e-3) / 1e12, 1),
+                                "us_back_to_back": round(t["ms_ref_b2b"] * 1e3, 2)},
+             "time_vs_side_reference": round(ms / ms_ref, 3),
+             "time_vs_side_reference_back_to_back": round(t["ms_b2b"] / t["ms_ref_b2b"], 3)}
         out.append(e)
         del a, b, c, ws
 
@@ -720,19 +768,23 @@ def run_configs(cb, dev, stream, reps: int) -> list[dict]:
     o = torch.empty(32, 56, 56, 256, device=dev, dtype=torch.float16)
     d = cb.conv_desc(x, wt, o, stride=1, padding=1, bias=bias, relu=True)
     q = cb.conv2d_query(d)
-    ms = median_launch_ms(lambda: cb.conv2d_desc(d, stream=stream), stream, flush, reps)
-    cb.sync_status(stream)
     xc = x.permute(0, 3, 1, 2)       # NCHW view of the NHWC data (channels-last)
     wc = wt.permute(0, 3, 1, 2)      # KCRS view of KRSC
-    ms_ref = median_launch_ms(lambda: Fn.conv2d(xc, wc, bias, stride=1, padding=1), stream, flush, reps)
+    t = ab_timing(cb, lambda: cb.conv2d_desc(d, stream=stream), lambda: Fn.conv2d(xc, wc, bias, stride=1, padding=1),
+                  stream, flush, reps, probe)
+    cb.sync_status(stream)
+    ms, ms_ref = t["ms"], t["ms_ref"]
     flops = 2.0 * 32 * 56 * 56 * 256 * 2304
     tf = flops / (ms * 1e-3) / 1e12
     out.append({"config": "5", "workload": "conv2d_f16_n32_56x56_c256_k256_3x3_bias_relu", "kernel": kernel_name(q),
                 "launches": 1, "us": round(ms * 1e3, 2), "tflops": round(tf, 1), "bound": "tensor",
                 "frac": round(tf / peak, 4),
+                "us_back_to_back": round(t["ms_b2b"] * 1e3, 2), "effective_sm_mhz": t["mhz"] and round(t["mhz"]),
                 "side_reference": {"what": "cuDNN via torch conv2d, channels-last fp16, bias, no ReLU",
-                                   "us": round(ms_ref * 1e3, 2), "tflops": round(flops / (ms_ref * 1e-3) / 1e12, 1)},
-                "time_vs_side_reference": round(ms / ms_ref, 3)})
+                                   "us": round(ms_ref * 1e3, 2), "tflops": round(flops / (ms_ref * 1e-3) / 1e12, 1),
+                                   "us_back_to_back": round(t["ms_ref_b2b"] * 1e3, 2)},
+                "time_vs_side_reference": round(ms / ms_ref, 3),
+                "time_vs_side_reference_back_to_back": round(t["ms_b2b"] / t["ms_ref_b2b"], 3)})
     for e in out:
         e["peak_source"] = peak_src if e["bound"] == "tensor" else "measured (copy)"
     return out
@@ -809,14 +861,15 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
 
     # ---------------------------------------------------------- end to end from pinned host buffers
     e2e_steps = max(1, min(args.steps, 20))
+    e2e_fn = case.e2e_step or (lambda: None)
     for _ in range(max(1, min(args.warmup, 3))):
-        case.e2e_step()
+        e2e_fn()
     barrier()
     t_wall2 = time.time()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
     for _ in range(e2e_steps):
-        case.e2e_step()
+        e2e_fn()
     e3.record(stream)
     barrier()
     t_wall3 = time.time()
@@ -887,9 +940,10 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
         "config": config_block(spec, world),
         "kernel": case.kernel,
         "roofline": roof,
-        "e2e": {"value": e2e_value, "unit": unit, "h2d_bytes_per_step": case.h2d, "d2h_bytes_per_step": case.d2h,
-                "steps": e2e_steps, "ms_per_step": ms_e2e_max / e2e_steps,
-                "h2d_gbs_per_rank": case.h2d / (ms_e2e_max / e2e_steps * 1e-3) / 1e9, **case.e2e_info},
+        "e2e": None if case.e2e_step is None else {
+            "value": e2e_value, "unit": unit, "h2d_bytes_per_step": case.h2d, "d2h_bytes_per_step": case.d2h,
+            "steps": e2e_steps, "ms_per_step": ms_e2e_max / e2e_steps,
+            "h2d_gbs_per_rank": case.h2d / (ms_e2e_max / e2e_steps * 1e-3) / 1e9, **case.e2e_info},
         "gpu_launches": args.steps * case.launches_per_step,
         "clocks": clocks,
         "cpu_baseline": cpu,
@@ -932,6 +986,8 @@ def main() -> None:
                     choices=["auto", "sharded", "gemm8192", "custom", "smallk", "conv", "relu"])
     ap.add_argument("--shape", default=None, help="MxNxK for --workload custom")
     ap.add_argument("--dtype", default="f16", choices=["f16", "bf16"], help="input/output type for --workload custom")
+    ap.add_argument("--layout", default="NN", choices=["NN", "NT", "TN", "TT"],
+                    help="storage of A and B for --workload custom (T: A stored K x M / B stored N x K)")
     ap.add_argument("--tile", default=None,
                     help="force a kernel configuration: wide256, pair256, pair128, single256, single128 or single64")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -943,7 +999,7 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     wl = args.workload if args.workload != "auto" else "sharded"
-    spec = workload_spec(wl, args.shape, args.dtype)
+    spec = workload_spec(wl, args.shape, args.dtype, args.layout)
 
     if args.impl == "reference":
         bench_reference(args, spec, world, rank)
