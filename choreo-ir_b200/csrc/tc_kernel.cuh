@@ -126,6 +126,22 @@ __device__ __forceinline__ float load_bias(const void* bias, int dt, int idx) {
   return __half2float(static_cast<const __half*>(bias)[idx]);
 }
 
+// Bias values one epilogue warp needs for a tile, loaded before it waits for
+// the accumulator so the load latency hides behind the wait: lane j holds
+// column n_first + 32 c + j for chunk c (0 past N or without a bias).
+template <int kCols>
+struct BiasRegs {
+  float v[kCols / 32];
+};
+template <int kCols>
+__device__ __forceinline__ void bias_prefetch(BiasRegs<kCols>& br, int n_first, const TcParams& p, int lane) {
+#pragma unroll
+  for (int c = 0; c < kCols / 32; ++c) {
+    const int n = n_first + 32 * c + lane;
+    br.v[c] = (p.bias != nullptr && n < p.n) ? load_bias(p.bias, p.dtype_bias, n) : 0.f;
+  }
+}
+
 __device__ __forceinline__ uint64_t l2_policy(int code) {
   return code == 1 ? l2_policy_evict_last() : (code == 2 ? l2_policy_evict_first() : l2_policy_evict_normal());
 }
@@ -237,6 +253,48 @@ __device__ __forceinline__ void stage_row_32(const float (&v)[32], uint32_t row_
   }
 }
 
+__device__ __forceinline__ float4 ld_shared_v4_f32(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+// (d0, d1) = (a0, a1) * s + (c0, c1) with one packed fp32 FMA (one rounding
+// per element).
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float s, float c0, float c1) {
+  uint64_t a, b, c, d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(b) : "f"(s));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(c) : "f"(c0), "f"(c1));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+
+// ReLU on a packed pair of 16-bit values: max(x, +0) with NaN kept NaN.
+__device__ __forceinline__ uint32_t relu2(uint32_t x, __half*) {
+  uint32_t r;
+  asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(0u));
+  return r;
+}
+__device__ __forceinline__ uint32_t relu2(uint32_t x, __nv_bfloat16*) {
+  uint32_t r;
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(0u));
+  return r;
+}
+
+// Writes 32 values of this thread's row, already packed as 16 16-bit pairs,
+// into the 128-byte-swizzled staging row at 16-byte chunk `chunk0`.
+__device__ __forceinline__ void stage_packed_32(const uint32_t (&q)[16], uint32_t row_addr, int lane, int chunk0) {
+  const int sw = lane & 7;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    st_shared_v4(row_addr + (((chunk0 + j) ^ sw) << 4), q[4 * j + 0], q[4 * j + 1], q[4 * j + 2], q[4 * j + 3]);
+}
+
 // Epilogue for one 32-column chunk of one row held by this thread (direct
 // global stores: 16-byte vectors where legal, scalars at ragged edges).
 template <typename OutT>
@@ -277,16 +335,23 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], OutT* cr
 // Epilogue of one warp: 32 accumulator rows (the TMEM lanes of the warp's
 // quarter) x kCols columns at TMEM address `taddr`, written to output rows
 // row0 .. row0 + 31 and columns n_first .. n_first + kCols of batch item b.
-// Columns are read from TMEM in batches of 64 (two tcgen05.ld per wait);
-// `release` hands the accumulator back to the MMA issuer right after the last
-// batch is in registers, before its arithmetic and stores, so the next tile's
-// MMAs overlap them. With a TMA-addressable C the rows leave through the
-// warp's 4 KB staging buffer as bulk tensor stores of 128-byte rows (clipped
-// by the tensor map at the matrix edges); otherwise as 16-byte vector stores.
+// `release` hands the accumulator back to the MMA issuer, which waits for it
+// before the next tile's MMAs into the same columns, so the work before it is
+// on the MMA pipe's critical path.
+//  - 16-bit output through the TMA store without a beta * C term (the common
+//    case): every column is read from TMEM, scaled, biased (bias prefetched in
+//    `br`), clamped and packed to 16-bit pairs in registers, then the
+//    accumulator is released, and only then are the rows staged in the warp's
+//    4 KB buffer and sent as bulk tensor stores of 128-byte rows (clipped by
+//    the tensor map at the matrix edges).
+//  - otherwise columns are read in batches of 64 (two tcgen05.ld per wait),
+//    the accumulator is released once the last batch is in registers, and the
+//    arithmetic and stores follow batch by batch (staging + bulk tensor stores
+//    when C is TMA-addressable, else 16-byte vector stores).
 template <int kCols, typename OutT, typename Release>
 __device__ __forceinline__ void epilogue_warp(uint32_t taddr, int n_first, int row0, int b, const TcParams& p,
                                               const CUtensorMap* tma_c, uint32_t stage_buf, int lane,
-                                              Release&& release) {
+                                              const BiasRegs<kCols>& br, Release&& release) {
   constexpr int kBatch = kCols < 64 ? kCols / 32 : 2;  // 32-column chunks per tcgen05.wait::ld
   constexpr int kBatches = kCols / 32 / kBatch;
   constexpr int E = 128 / static_cast<int>(sizeof(OutT));  // columns per 128-byte staging row
@@ -302,11 +367,71 @@ __device__ __forceinline__ void epilogue_warp(uint32_t taddr, int n_first, int r
     release();
     return;
   }
+  const bool use_tma = kTmaOk && p.c_tma != 0;
+  if constexpr (sizeof(OutT) == 2 && kTmaOk) {
+    if (use_tma && p.beta == 0.f) {
+      constexpr int kChunks = kCols / 32;
+      const bool has_bias = p.bias != nullptr;
+      if (has_bias) {
+        // The warp's kCols bias values go to the head of its staging buffer
+        // (free until the stores below) and are read back as broadcast
+        // vector loads: no cross-lane shuffles in the arithmetic.
+        if (lane == 0) bulk_wait_read_all();  // the warp's previous store has read the buffer
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) st_shared_f32(stage_buf + static_cast<uint32_t>(c * 32 + lane) * 4u, br.v[c]);
+        __syncwarp();
+      }
+      uint32_t q[kChunks][16];
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        if (n_first + 32 * c < p.n) {  // warp-uniform
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 bv = has_bias ? ld_shared_v4_f32(stage_buf + static_cast<uint32_t>(c * 32 + 4 * j) * 4u)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+            float v0, v1, v2, v3;
+            fma2(v0, v1, __uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), p.alpha, bv.x, bv.y);
+            fma2(v2, v3, __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]), p.alpha, bv.z, bv.w);
+            q[c][2 * j] = pack2(v0, v1, static_cast<OutT*>(nullptr));
+            q[c][2 * j + 1] = pack2(v2, v3, static_cast<OutT*>(nullptr));
+          }
+          if (p.relu) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) q[c][i] = relu2(q[c][i], static_cast<OutT*>(nullptr));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) q[c][i] = 0u;
+        }
+      }
+      release();
+      const uint32_t row_addr = stage_buf + static_cast<uint32_t>(lane) * 128u;
+#pragma unroll
+      for (int g = 0; g < kChunks / kCpg; ++g) {
+        const int n_base = n_first + g * E;
+        if (n_base >= p.n) break;  // warp-uniform
+        if (lane == 0) bulk_wait_read_all();  // the warp's previous store has read the buffer
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < kCpg; ++c) stage_packed_32(q[g * kCpg + c], row_addr, lane, c * 4);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(tma_c, stage_buf, n_base, row0, b);
+          bulk_commit_group();
+        }
+      }
+      return;
+    }
+  }
   const int row = row0 + lane;
   const bool row_ok = row < p.m;
   OutT* crow = static_cast<OutT*>(p.c) + static_cast<int64_t>(b) * p.stride_c +
                static_cast<int64_t>(row_ok ? row : 0) * p.ldc;
-  const bool use_tma = kTmaOk && p.c_tma != 0;
 #pragma unroll 1
   for (int bi = 0; bi < kBatches; ++bi) {
     if (bi >= valid) break;  // warp-uniform
@@ -509,18 +634,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int64_t t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
       const uint32_t buf = local & 1;
       const uint32_t tph = (local >> 1) & 1;
+      int b, mb, nb;
+      tile_coords(t, p, b, mb, nb);
+      const int n_first = nb * BN + col_half * (BN / 2);
+      BiasRegs<BN / 2> br;
+      bias_prefetch(br, n_first, p, lane);
       int ready = 0;
       if (lane == 0)
         ready = mbar_wait(smem_u32(&bars->tmem_full[buf]), tph, wctx, kStatusTimeoutEpilogue) ? 1 : 0;
       ready = __shfl_sync(0xffffffffu, ready, 0);
       if (!ready) break;
       tc_fence_after();
-      int b, mb, nb;
-      tile_coords(t, p, b, mb, nb);
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN + col_half * (BN / 2);
-      epilogue_warp<BN / 2, OutT>(taddr, nb * BN + col_half * (BN / 2), mb * kBM + quarter * 32, b, p, &tma_c,
-                                  stage_buf, lane, [&] {
+      epilogue_warp<BN / 2, OutT>(taddr, n_first, mb * kBM + quarter * 32, b, p, &tma_c, stage_buf, lane, br, [&] {
                                     tc_fence_before();
                                     __syncwarp();
                                     if (lane == 0) mbar_arrive(smem_u32(&bars->tmem_empty[buf]));
@@ -711,19 +838,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int64_t t = cluster_id; t < p.num_tiles; t += num_clusters, ++local) {
       const uint32_t buf = local & 1;
       const uint32_t tph = (local >> 1) & 1;
+      int b, mb, nb;
+      tile_coords(t, p, b, mb, nb);
+      const int n_first = nb * BN + col_half * (BN / 2);
+      BiasRegs<BN / 2> br;
+      bias_prefetch(br, n_first, p, lane);
       int ready = 0;
       if (lane == 0)
         ready = mbar_wait(smem_u32(&bars->tmem_full[buf]), tph, wctx, kStatusTimeoutEpilogue) ? 1 : 0;
       ready = __shfl_sync(0xffffffffu, ready, 0);
       if (!ready) break;
       tc_fence_after();
-      int b, mb, nb;
-      tile_coords(t, p, b, mb, nb);
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN + col_half * (BN / 2);
-      epilogue_warp<BN / 2, OutT>(taddr, nb * BN + col_half * (BN / 2),
-                                  mb * (2 * kBM) + static_cast<int>(rank) * kBM + quarter * 32, b, p, &tma_c,
-                                  stage_buf, lane, [&] {
+      epilogue_warp<BN / 2, OutT>(taddr, n_first, mb * (2 * kBM) + static_cast<int>(rank) * kBM + quarter * 32, b,
+                                  p, &tma_c, stage_buf, lane, br, [&] {
                                     tc_fence_before();
                                     __syncwarp();
                                     if (lane == 0) {
@@ -998,6 +1127,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int64_t t = cluster_id; t < p.num_tiles && ok; t += num_clusters, ++local) {
       int b, mb, nb;
       tile_coords(t, p, b, mb, nb);
+      const int n_first = nb * BN + col_half * (BN / 2);  // the same columns for both halves
+      BiasRegs<BN / 2> br;
+      bias_prefetch(br, n_first, p, lane);
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         int ready = 0;
@@ -1011,9 +1143,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t taddr =
             tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + h * BN + col_half * (BN / 2);
-        epilogue_warp<BN / 2, OutT>(taddr, nb * BN + col_half * (BN / 2),
+        epilogue_warp<BN / 2, OutT>(taddr, n_first,
                                     mb * (4 * kBM) + static_cast<int>(rank) * (2 * kBM) + h * kBM + quarter * 32,
-                                    b, p, &tma_c, stage_buf, lane, [&] {
+                                    b, p, &tma_c, stage_buf, lane, br, [&] {
                                       tc_fence_before();
                                       __syncwarp();
                                       if (lane == 0) {
