@@ -12,7 +12,8 @@ distributions; nothing is read from disk):
             included, so the 1 -> N curve compares one workload.
   gemm8192  fp16 GEMM C[8192x8192] = A[8192x8192] B[8192x8192], row-major,
             U[-1,1], fp32 accumulation, fp16 output.
-  custom    GEMM of --shape MxNxK and --dtype (U[-1,1], NN).
+  custom    GEMM of --shape MxNxK and --dtype (U[-1,1]), stored as --layout
+            (NN default), with a fused bias + ReLU when --bias-relu is given.
   smallk    fp16 GEMM 16384 x 16384 x 128: output-write (HBM) bound.
   conv      implicit-GEMM conv2d NHWC fp16, N=32, 56x56, C=K=256, 3x3, s1 p1,
             activations U[0,1], weights N(0, 1/48), bias N(0, 0.1) + ReLU; at
@@ -89,11 +90,12 @@ def _gemm(workload, m, n, k, dtype, dist, bias, relu, layout="NN"):
                 relu=relu, layout=layout)
 
 
-def workload_spec(name: str, shape: str | None = None, dtype: str = "f16", layout: str = "NN") -> dict:
+def workload_spec(name: str, shape: str | None = None, dtype: str = "f16", layout: str = "NN",
+                  bias_relu: bool = False) -> dict:
     if name == "custom":
         m, n, k = (int(x) for x in (shape or "4096x4096x4096").lower().split("x"))
-        suffix = "" if layout == "NN" else f"_{layout}"
-        return _gemm(f"gemm_{dtype}_{m}x{n}x{k}{suffix}", m, n, k, dtype, "U[-1,1]", False, False, layout)
+        suffix = ("" if layout == "NN" else f"_{layout}") + ("_bias_relu" if bias_relu else "")
+        return _gemm(f"gemm_{dtype}_{m}x{n}x{k}{suffix}", m, n, k, dtype, "U[-1,1]", bias_relu, bias_relu, layout)
     if name == "gemm8192":
         return _gemm("gemm_f16_8192x8192x8192", 8192, 8192, 8192, "f16", "U[-1,1]", False, False)
     if name == "sharded":
@@ -431,6 +433,7 @@ class Case:
     """Device buffers and the step functions of one workload on one rank."""
     step = None        # one launch on device-resident inputs
     e2e_step = None    # host->device inputs, the launch, device->host output
+    floor_step = None  # the same host<->device copies with no kernel
     h2d = d2h = 0
     rows = None        # this rank's slab (GEMM rows)
     units_total = 0.0  # whole-job FLOPs (or bytes) per step
@@ -446,6 +449,29 @@ def _pinned_copy(t):
     h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
     h.copy_(t)
     return h
+
+
+def _copy_floor(stream, dev, ins, outs):
+    """The transfers of one end-to-end step and nothing else: every (device,
+    pinned host) pair in `ins` copied in on one stream while every (host,
+    device) pair in `outs` is copied out on another. Its time is the floor
+    the host links put under the end-to-end step (the same bytes, no kernel)."""
+    import torch
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def step():
+        s_in.wait_stream(stream)
+        s_out.wait_stream(stream)
+        with torch.cuda.stream(s_in):
+            for d, h in ins:
+                if d is not None and d.numel():
+                    d.copy_(h, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            for h, d in outs:
+                h.copy_(d, non_blocking=True)
+        stream.wait_stream(s_in)
+        stream.wait_stream(s_out)
+    return step
 
 
 def kernel_name(q) -> str:
@@ -530,6 +556,9 @@ def setup_gemm(cb, spec, world, rank, dev, stream) -> Case:
                                  f"from {share} host rows per rank by an NCCL all-gather (inside the timed "
                                  f"region); bias copied in per step"}
     case.d2h = c_h.numel() * c_h.element_size()
+    b_rows = (0, K) if world == 1 else (k0, k1)
+    case.floor_step = _copy_floor(stream, dev, [(a, a_h), (b[b_rows[0]:b_rows[1]], b_h[b_rows[0]:b_rows[1]]),
+                                                (bias, bias_h)], [(c_h, c)])
     case.rows = rows
     case.b_dev, case.c_dev = b, c
     case.flops, case.bytes_ = spec_flops_bytes(spec, rows)
@@ -565,6 +594,7 @@ def setup_conv(cb, spec, world, rank, dev, stream) -> Case:
     case.e2e_step = lambda: plan.run(x_h, w_h, o_h, b_h, stream=stream)
     case.h2d = sum(t.numel() * t.element_size() for t in (x_h, w_h, b_h))
     case.d2h = o_h.numel() * o_h.element_size()
+    case.floor_step = _copy_floor(stream, dev, [(x, x_h), (wt, w_h), (bias, b_h)], [(o_h, out)])
     case.flops, case.bytes_ = spec_flops_bytes({**spec, "n": imgs})
     case.units_total = spec_flops_bytes(spec)[0]
     case.flush = flushes_l2(spec, world)
@@ -880,14 +910,28 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
         sampler.mark(t_wall2, t_wall3)
         clocks = sampler.stop()
 
+    # ---------------------------------------------------------- the end-to-end step's copies alone (its floor)
+    ms_floor = 0.0
+    if case.floor_step is not None:
+        for _ in range(2):
+            case.floor_step()
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(e2e_steps):
+            case.floor_step()
+        f1.record(stream)
+        barrier()
+        ms_floor = f0.elapsed_time(f1)
+
     # ---------------------------------------------------------- the sharded GEMM's exchanges, timed apart
     exchange = time_exchanges(case, world, rank, dev, stream) if world > 1 and spec["kind"] == "gemm" else None
 
     # ---------------------------------------------------------- max over ranks
-    t = torch.tensor([ms, ms_e2e], device=dev, dtype=torch.float64)
+    t = torch.tensor([ms, ms_e2e, ms_floor], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max, ms_e2e_max = float(t[0]), float(t[1])
+    ms_max, ms_e2e_max, ms_floor_max = float(t[0]), float(t[1]), float(t[2])
     scale = 1e9 if unit == "GB/s" else 1e12
     value = case.units_total * args.steps / (ms_max * 1e-3) / scale
     e2e_value = case.units_total * e2e_steps / (ms_e2e_max * 1e-3) / scale
@@ -906,6 +950,16 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
     roof["traffic"] = profiled_traffic(spec["workload"], case.rows)
     roof["per_launch_ms"] = per_launch_ms
     roof["kernel"] = case.kernel.get("name")
+    if roof["bound"] == "tensor" and clk[1] > 0:
+        # What the SMs could do at the clock the launches actually ran at: 8192
+        # dense f16/bf16 FLOP per SM per cycle (a 256 x 256 x 64 k-block of one
+        # CTA takes 1024 tensor-pipe cycles), times the SM count.
+        mhz = 1e3 * clk[0] / clk[1]
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        roof["clock_limited_peak"] = sms * 8192 * mhz * 1e6 / 1e12
+        roof["frac_of_clock_limited_peak"] = roof["achieved"] / roof["clock_limited_peak"]
+        roof["clock_limited_how"] = (f"{sms} SMs x 8192 FLOP/cycle x the effective SM clock of the timed launches "
+                                     f"({mhz:.0f} MHz, in-kernel %clock64 / %globaltimer)")
 
     configs = None
     if world == 1 and not args.no_configs:
@@ -943,7 +997,14 @@ def bench_choreo(args, spec: dict, world: int, rank: int, local_rank: int) -> No
         "e2e": None if case.e2e_step is None else {
             "value": e2e_value, "unit": unit, "h2d_bytes_per_step": case.h2d, "d2h_bytes_per_step": case.d2h,
             "steps": e2e_steps, "ms_per_step": ms_e2e_max / e2e_steps,
-            "h2d_gbs_per_rank": case.h2d / (ms_e2e_max / e2e_steps * 1e-3) / 1e9, **case.e2e_info},
+            "h2d_gbs_per_rank": case.h2d / (ms_e2e_max / e2e_steps * 1e-3) / 1e9,
+            "copy_floor_ms_per_step": ms_floor_max / e2e_steps if ms_floor_max else None,
+            "copy_floor_gbs_per_rank": ((case.h2d + case.d2h) / (ms_floor_max / e2e_steps * 1e-3) / 1e9
+                                        if ms_floor_max else None),
+            "frac_of_copy_floor": (ms_floor_max / ms_e2e_max) if ms_floor_max else None,
+            "copy_floor_how": "the step's host<->device copies alone (inputs in on one stream, output out on "
+                              "another, no kernel), max over ranks",
+            **case.e2e_info},
         "gpu_launches": args.steps * case.launches_per_step,
         "clocks": clocks,
         "cpu_baseline": cpu,
@@ -986,6 +1047,7 @@ def main() -> None:
                     choices=["auto", "sharded", "gemm8192", "custom", "smallk", "conv", "relu"])
     ap.add_argument("--shape", default=None, help="MxNxK for --workload custom")
     ap.add_argument("--dtype", default="f16", choices=["f16", "bf16"], help="input/output type for --workload custom")
+    ap.add_argument("--bias-relu", action="store_true", help="fused bias + ReLU epilogue for --workload custom")
     ap.add_argument("--layout", default="NN", choices=["NN", "NT", "TN", "TT"],
                     help="storage of A and B for --workload custom (T: A stored K x M / B stored N x K)")
     ap.add_argument("--tile", default=None,
@@ -999,7 +1061,7 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     wl = args.workload if args.workload != "auto" else "sharded"
-    spec = workload_spec(wl, args.shape, args.dtype, args.layout)
+    spec = workload_spec(wl, args.shape, args.dtype, args.layout, args.bias_relu)
 
     if args.impl == "reference":
         bench_reference(args, spec, world, rank)
