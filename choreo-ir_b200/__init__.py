@@ -65,6 +65,7 @@ class Tuning(C.Structure):
     _fields_ = [
         ("tile", C.c_char * 16), ("split_k", C.c_int32), ("group_m", C.c_int32),
         ("l2_policy_a", C.c_int32), ("l2_policy_b", C.c_int32), ("wait_timeout_ms", C.c_double),
+        ("handover_kb", C.c_int32), ("reserved", C.c_int32),
     ]
 
 
@@ -413,7 +414,7 @@ def get_tuning() -> Tuning:
 
 
 def set_tuning(*, tile: str = "", split_k: int = 0, group_m: int = 0, l2_policy_a: int = -1,
-               l2_policy_b: int = -1, wait_timeout_ms: float = 0.0) -> None:
+               l2_policy_b: int = -1, wait_timeout_ms: float = 0.0, handover_kb: int = 0) -> None:
     """Installs dispatcher overrides (choreo_tuning_set); the defaults leave
     every choice to the library."""
     t = Tuning()
@@ -421,6 +422,7 @@ def set_tuning(*, tile: str = "", split_k: int = 0, group_m: int = 0, l2_policy_
     t.split_k, t.group_m = split_k, group_m
     t.l2_policy_a, t.l2_policy_b = l2_policy_a, l2_policy_b
     t.wait_timeout_ms = wait_timeout_ms
+    t.handover_kb = handover_kb
     check(lib.choreo_tuning_set(C.byref(t)))
 
 

@@ -107,7 +107,7 @@ namespace {
 // Process-wide tuning settings. Readers keep a per-thread copy and refresh it
 // only when the generation moves, so the common path takes no lock.
 std::mutex g_tuning_mu;
-choreo_tuning g_tuning = {{0}, 0, 0, -1, -1, 0.0};
+choreo_tuning g_tuning = {{0}, 0, 0, -1, -1, 0.0, 0, 0};
 std::atomic<uint64_t> g_tuning_gen{1};
 
 bool known_tile(const char* s) {
@@ -119,7 +119,7 @@ bool known_tile(const char* s) {
 }  // namespace
 
 Tuning tuning() {
-  thread_local Tuning cached{{{0}, 0, 0, -1, -1, 0.0}, 0};
+  thread_local Tuning cached{{{0}, 0, 0, -1, -1, 0.0, 0, 0}, 0};
   const uint64_t gen = g_tuning_gen.load(std::memory_order_acquire);
   if (cached.generation != gen) {
     std::lock_guard<std::mutex> lk(g_tuning_mu);
@@ -433,7 +433,7 @@ int choreo_sync_status(void* stream) {
 }
 
 int choreo_tuning_set(const choreo_tuning* t) {
-  choreo_tuning v = {{0}, 0, 0, -1, -1, 0.0};
+  choreo_tuning v = {{0}, 0, 0, -1, -1, 0.0, 0, 0};
   if (t != nullptr) {
     v = *t;
     v.tile[sizeof(v.tile) - 1] = 0;
@@ -446,6 +446,9 @@ int choreo_tuning_set(const choreo_tuning* t) {
       return fail(CHOREO_ERR_INVALID_ARG, "tuning: L2 policy codes are -1, 0, 1 or 2");
     if (!(v.wait_timeout_ms >= 0.0) || v.wait_timeout_ms > 3.6e6)
       return fail(CHOREO_ERR_INVALID_ARG, "tuning: wait_timeout_ms outside 0..3.6e6");
+    if (v.handover_kb < 0 || v.handover_kb > 64)
+      return fail(CHOREO_ERR_INVALID_ARG, "tuning: handover_kb %d outside 0..64", v.handover_kb);
+    v.reserved = 0;
   }
   {
     std::lock_guard<std::mutex> lk(g_tuning_mu);

@@ -280,6 +280,7 @@ int launch_conv_tc(const choreo_conv_desc& d, cudaStream_t stream) {
   kp.status = status_word();
   kp.timeout_ns = wait_timeout_ns();
   kp.clock_probe = clock_probe();
+  kp.handover_kb = tuning().t.handover_kb;
   if (kp.status == nullptr) return CHOREO_ERR_CUDA;
   const int grid = conv_grid(cfg, kp.num_tiles);
   switch (d.dtype_out) {

@@ -368,6 +368,7 @@ int launch_gemm_tc(const TcProblem& p, const TcConfig& cfg, cudaStream_t stream)
   kp.status = status_word();
   kp.timeout_ns = wait_timeout_ns();
   kp.clock_probe = clock_probe();
+  kp.handover_kb = tuning().t.handover_kb;
   if (kp.status == nullptr) return CHOREO_ERR_CUDA;
 
   const int sms = current_sm_count();

@@ -67,6 +67,9 @@ struct TcParams {
   // failure reporting
   uint32_t* status;
   uint64_t timeout_ns;
+  // wide tile: k-blocks replayed around each accumulator hand-over (0 = the
+  // pipeline depth)
+  int32_t handover_kb;
   // measurement hook (null = off): CTA 0 adds the SM clock cycles and the
   // %globaltimer nanoseconds of its lifetime to [0] and [1], and 1 to [2]
   unsigned long long* clock_probe;
@@ -274,16 +277,40 @@ __device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, f
   asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
 }
 
-// ReLU on a packed pair of 16-bit values: max(x, +0) with NaN kept NaN.
-__device__ __forceinline__ uint32_t relu2(uint32_t x, __half*) {
+// Round a pair to 16 bits with ReLU folded into the conversion (cvt .relu:
+// negative results become 0, NaN stays NaN); a lands in the low half.
+__device__ __forceinline__ uint32_t pack2_relu(float a, float b, __half*) {
   uint32_t r;
-  asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(0u));
+  asm("cvt.rn.relu.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
   return r;
 }
-__device__ __forceinline__ uint32_t relu2(uint32_t x, __nv_bfloat16*) {
+__device__ __forceinline__ uint32_t pack2_relu(float a, float b, __nv_bfloat16*) {
   uint32_t r;
-  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(0u));
+  asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
   return r;
+}
+
+// One 32-column chunk of the 16-bit epilogue: alpha * acc + bias (bias read
+// as broadcasts from `bias_s`, the chunk's 32 values; none when null),
+// rounded to 16-bit pairs, with ReLU folded into the rounding when RELU.
+template <typename OutT, bool RELU>
+__device__ __forceinline__ void convert_chunk(const uint32_t (&r)[32], float alpha, uint32_t bias_s, bool has_bias,
+                                              uint32_t (&q)[16]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 bv = has_bias ? ld_shared_v4_f32(bias_s + static_cast<uint32_t>(4 * j) * 4u)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+    float v0, v1, v2, v3;
+    fma2(v0, v1, __uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), alpha, bv.x, bv.y);
+    fma2(v2, v3, __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]), alpha, bv.z, bv.w);
+    if constexpr (RELU) {
+      q[2 * j] = pack2_relu(v0, v1, static_cast<OutT*>(nullptr));
+      q[2 * j + 1] = pack2_relu(v2, v3, static_cast<OutT*>(nullptr));
+    } else {
+      q[2 * j] = pack2(v0, v1, static_cast<OutT*>(nullptr));
+      q[2 * j + 1] = pack2(v2, v3, static_cast<OutT*>(nullptr));
+    }
+  }
 }
 
 // Writes 32 values of this thread's row, already packed as 16 16-bit pairs,
@@ -389,20 +416,11 @@ __device__ __forceinline__ void epilogue_warp(uint32_t taddr, int n_first, int r
           uint32_t r[32];
           tmem_ld_32x32b_x32(taddr + c * 32, r);
           tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float4 bv = has_bias ? ld_shared_v4_f32(stage_buf + static_cast<uint32_t>(c * 32 + 4 * j) * 4u)
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-            float v0, v1, v2, v3;
-            fma2(v0, v1, __uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), p.alpha, bv.x, bv.y);
-            fma2(v2, v3, __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]), p.alpha, bv.z, bv.w);
-            q[c][2 * j] = pack2(v0, v1, static_cast<OutT*>(nullptr));
-            q[c][2 * j + 1] = pack2(v2, v3, static_cast<OutT*>(nullptr));
-          }
-          if (p.relu) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) q[c][i] = relu2(q[c][i], static_cast<OutT*>(nullptr));
-          }
+          const uint32_t bias_s = stage_buf + static_cast<uint32_t>(c * 32) * 4u;
+          if (p.relu)
+            convert_chunk<OutT, true>(r, p.alpha, bias_s, has_bias, q[c]);
+          else
+            convert_chunk<OutT, false>(r, p.alpha, bias_s, has_bias, q[c]);
         } else {
 #pragma unroll
           for (int i = 0; i < 16; ++i) q[c][i] = 0u;
@@ -1041,7 +1059,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // epilogue has read half 0 out, and replayed for half 1 (then
         // released) once it has read half 1 — the half-1 drain overlaps
         // D k-blocks of half-0 MMAs.
-        const int D = p.num_k_blocks < STAGES ? p.num_k_blocks : STAGES;
+        const int W = p.handover_kb > 0 && p.handover_kb < STAGES ? p.handover_kb : STAGES;
+        const int D = p.num_k_blocks < W ? p.num_k_blocks : W;
         if (!mbar_wait(smem_u32(&bars->tmem_empty[0]), tph ^ 1, wctx, kStatusTimeoutMma)) {
           ok = false;
           break;
@@ -1075,7 +1094,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         // Steady state: both halves per stage, up to the tail.
-        const int T = (p.num_k_blocks - D) < STAGES ? (p.num_k_blocks - D) : STAGES;
+        const int T = (p.num_k_blocks - D) < W ? (p.num_k_blocks - D) : W;
         for (int kb = D; kb < p.num_k_blocks - T; ++kb) {
           if (!mbar_wait(smem_u32(&bars->full[stage]), phase, wctx, kStatusTimeoutMma)) {
             ok = false;

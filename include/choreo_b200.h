@@ -167,6 +167,10 @@ typedef struct choreo_tuning {
   int32_t l2_policy_a;      /* -1 = default (evict_last); 0 normal, 1 evict_last, 2 evict_first */
   int32_t l2_policy_b;      /* -1 = default (normal); same codes */
   double wait_timeout_ms;   /* 0 = default 2000: limit of every bounded pipeline wait */
+  int32_t handover_kb;      /* 512 x 256 tiles: k-blocks the MMA issuer runs for one accumulator
+                               half while the other is handed over, at each end of a tile
+                               (0 = the pipeline depth) */
+  int32_t reserved;
 } choreo_tuning;
 
 /* Installs *t for every later call from any host thread (NULL restores the
