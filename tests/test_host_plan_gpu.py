@@ -124,3 +124,71 @@ def test_host_conv_weights_on_device(cb, cuda, orc):
     ref = orc.conv2d_f64(x, wt, F16, bias=bias, dtype_bias=F16, relu=True)
     assert_close(as_f64(_bits(out), F16).reshape(-1, k), ref, what="host conv plan, weights on device", k=9 * c)
     plan.close()
+
+
+def test_host_gemm_f32_output_host_bias_many_parts(cb, cuda, orc):
+    """f16 inputs with f32 output and a bias of the input type read from the
+    host; 7 parts of 512 rows (the last shorter); the plan reused for
+    three runs queued back to back, each against fp64."""
+    import torch
+    m, n, k = 3300, 320, 704
+    plan = cb.HostGemmPlan(m, n, k, torch.float16, bias=True, relu=True, slabs=7, dtype_c=torch.float32)
+    assert [rows for _, rows in plan.slabs] == [512] * 6 + [228]
+    runs = []
+    for seed in (5, 6, 7):
+        gen = torch.Generator().manual_seed(seed)
+        a = torch.empty(m, k).uniform_(-1, 1, generator=gen).half().pin_memory()
+        b = torch.empty(k, n).uniform_(-1, 1, generator=gen).half().pin_memory()
+        bias = torch.empty(n).normal_(0, 0.5, generator=gen).half().pin_memory()
+        c = torch.full((m, n), -9.0, dtype=torch.float32).pin_memory()
+        plan.run(a, b, c, bias)
+        runs.append((a, b, bias, c))
+    torch.cuda.current_stream().synchronize()
+    cb.sync_status()
+    for a, b, bias, c in runs:
+        r = orc.gemm_f64(_bits(a), _bits(b), F16, bias=_bits(bias), dtype_bias=F16, relu=True)
+        assert_close(c.numpy().astype(np.float64), r, what="host GEMM plan f32 out", k=k)
+
+
+def test_clock_probe_counts_launches_and_reads_a_plausible_clock(cb, cuda):
+    """choreo_clock_probe_set: every tensor-core launch of this thread adds its
+    first CTA's cycles and nanoseconds and counts itself; the ratio is an SM
+    clock the B200 can run at; NULL turns it off; host memory is refused."""
+    import torch
+    probe = torch.zeros(3, dtype=torch.int64, device="cuda")
+    a = torch.empty(1024, 2048, device="cuda", dtype=torch.bfloat16).uniform_(-1, 1)
+    b = torch.empty(2048, 1024, device="cuda", dtype=torch.bfloat16).uniform_(-1, 1)
+    c = torch.empty(1024, 1024, device="cuda", dtype=torch.bfloat16)
+    cb.check(cb.lib.choreo_clock_probe_set(probe.data_ptr()))
+    try:
+        for _ in range(5):
+            cb.gemm(a, b, c)
+    finally:
+        cb.check(cb.lib.choreo_clock_probe_set(None))
+    cb.gemm(a, b, c)  # not counted
+    cb.sync_status()
+    cycles, ns, launches = probe.cpu().tolist()
+    assert launches == 5 and cycles > 0 and ns > 0
+    assert 200.0 < 1e3 * cycles / ns < 2500.0, 1e3 * cycles / ns
+    host = np.zeros(3, np.uint64)
+    assert cb.lib.choreo_clock_probe_set(host.ctypes.data) == cb.ERR_INVALID_ARG
+    assert cb.lib.choreo_clock_probe_set(probe.data_ptr() + 4) == cb.ERR_INVALID_ARG  # 8-byte alignment
+
+
+def test_handover_window_setting_keeps_results(cb, cuda):
+    """The wide tile's hand-over window (choreo_tuning::handover_kb) changes the
+    order MMAs are issued in, never the sums: every setting gives the same
+    bits as the default."""
+    import torch
+    m, n, k = 1536, 1024, 2048
+    a = torch.empty(m, k, device="cuda", dtype=torch.float16).uniform_(-1, 1)
+    b = torch.empty(k, n, device="cuda", dtype=torch.float16).uniform_(-1, 1)
+    with cb.tuning(tile="wide256"):
+        ref = torch.empty(m, n, device="cuda", dtype=torch.float16)
+        cb.gemm(a, b, ref)
+    for w in (1, 2, 3, 4, 9):
+        with cb.tuning(tile="wide256", handover_kb=w):
+            c = torch.empty_like(ref)
+            cb.gemm(a, b, c)
+        cb.sync_status()
+        assert torch.equal(c, ref), w
