@@ -409,24 +409,24 @@ __device__ __forceinline__ void epilogue_warp(uint32_t taddr, int n_first, int r
         for (int c = 0; c < kChunks; ++c) st_shared_f32(stage_buf + static_cast<uint32_t>(c * 32 + lane) * 4u, br.v[c]);
         __syncwarp();
       }
+      // Every chunk's TMEM read is in flight at once and waited for once; the
+      // accumulator goes back to the MMA issuer before the arithmetic.
+      // Columns past N are read and converted too (TMEM holds them; the
+      // tensor map clips them from the stores).
+      uint32_t r[kChunks][32];
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) tmem_ld_32x32b_x32(taddr + c * 32, r[c]);
+      tmem_wait_ld();
+      release();
       uint32_t q[kChunks][16];
 #pragma unroll
       for (int c = 0; c < kChunks; ++c) {
-        if (n_first + 32 * c < p.n) {  // warp-uniform
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(taddr + c * 32, r);
-          tmem_wait_ld();
-          const uint32_t bias_s = stage_buf + static_cast<uint32_t>(c * 32) * 4u;
-          if (p.relu)
-            convert_chunk<OutT, true>(r, p.alpha, bias_s, has_bias, q[c]);
-          else
-            convert_chunk<OutT, false>(r, p.alpha, bias_s, has_bias, q[c]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) q[c][i] = 0u;
-        }
+        const uint32_t bias_s = stage_buf + static_cast<uint32_t>(c * 32) * 4u;
+        if (p.relu)
+          convert_chunk<OutT, true>(r[c], p.alpha, bias_s, has_bias, q[c]);
+        else
+          convert_chunk<OutT, false>(r[c], p.alpha, bias_s, has_bias, q[c]);
       }
-      release();
       const uint32_t row_addr = stage_buf + static_cast<uint32_t>(lane) * 128u;
 #pragma unroll
       for (int g = 0; g < kChunks / kCpg; ++g) {
