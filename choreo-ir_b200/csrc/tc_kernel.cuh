@@ -1058,8 +1058,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // previous tile's epilogue ran) are consumed for half 0 as soon as the
         // epilogue has read half 0 out, and replayed for half 1 (then
         // released) once it has read half 1 — the half-1 drain overlaps
-        // D k-blocks of half-0 MMAs.
-        const int W = p.handover_kb > 0 && p.handover_kb < STAGES ? p.handover_kb : STAGES;
+        // D k-blocks of half-0 MMAs. The window defaults to the ring depth, one
+        // less for tiles under 64 k-blocks, whose stage refill at each tile
+        // boundary weighs more than a shorter overlap.
+        const int W = p.handover_kb > 0 && p.handover_kb < STAGES
+                          ? p.handover_kb
+                          : (p.num_k_blocks < 64 && STAGES > 2 ? STAGES - 1 : STAGES);
         const int D = p.num_k_blocks < W ? p.num_k_blocks : W;
         if (!mbar_wait(smem_u32(&bars->tmem_empty[0]), tph ^ 1, wctx, kStatusTimeoutMma)) {
           ok = false;

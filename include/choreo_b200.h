@@ -169,7 +169,8 @@ typedef struct choreo_tuning {
   double wait_timeout_ms;   /* 0 = default 2000: limit of every bounded pipeline wait */
   int32_t handover_kb;      /* 512 x 256 tiles: k-blocks the MMA issuer runs for one accumulator
                                half while the other is handed over, at each end of a tile
-                               (0 = the pipeline depth) */
+                               (0 = the pipeline depth, one less for tiles of fewer than
+                               64 k-blocks) */
   int32_t reserved;
 } choreo_tuning;
 
