@@ -115,6 +115,18 @@ int make_queues(choreo_host_plan* p) {
   return CHOREO_OK;
 }
 
+// The library's part count: every part moves at least kMinPartBytes over the
+// host links (in + out), at most 16 parts. More parts shorten the pipeline's
+// ends (the first copy in and the last copy out run alone) but each adds a
+// launch and cross-stream waits; on a B200 over PCIe 5 (55 GB/s in, 57 GB/s
+// out) the 2.3 GB config-4 GEMM step was fastest at 16 parts (25.2 ms, from
+// 25.3 at 8 and 25.7 at 32) and the 103 MB 32-image conv step at 2-3 runs
+// (1.27 ms, from 1.42 at 8).
+constexpr int64_t kMinPartBytes = 40ll << 20;
+int64_t default_parts(int64_t bytes_moved, int64_t units) {
+  return std::max<int64_t>(1, std::min<int64_t>({16, bytes_moved / kMinPartBytes, units}));
+}
+
 // Contiguous parts of `total` units: `parts` of them, each a multiple of
 // `align` units (only the last may be shorter).
 void split_parts(choreo_host_plan* p, int64_t total, int64_t parts, int64_t align) {
@@ -272,9 +284,10 @@ int choreo_host_gemm_plan_create(const choreo_host_gemm_desc* d, choreo_host_pla
   p->kind = 1;
   p->device = d->device;
   p->g = *d;
-  const int64_t parts = d->parts > 0 ? d->parts : std::max<int64_t>(1, std::min<int64_t>(16, d->m / 1024));
-  split_parts(p, d->m, parts, d->m >= 512 ? 512 : 1);  // whole wide-tile row blocks
   const int64_t eab = bytes_of(d->dtype_ab), ec = bytes_of(d->dtype_c);
+  const int64_t moved = d->m * d->k * eab + d->k * d->n * eab + d->m * d->n * ec;
+  const int64_t parts = d->parts > 0 ? d->parts : default_parts(moved, (d->m + 511) / 512);
+  split_parts(p, d->m, parts, d->m >= 512 ? 512 : 1);  // whole wide-tile row blocks
   int rc;
   if ((rc = alloc(&p->a, d->m * d->k * eab, &p->device_bytes, "A")) ||
       (rc = alloc(&p->b, d->k * d->n * eab, &p->device_bytes, "B")) ||
@@ -327,9 +340,11 @@ int choreo_host_conv_plan_create(const choreo_conv_desc* d, int32_t parts, int32
   p->cv = *d;
   p->conv_p = pp;
   p->conv_q = qq;
-  const int64_t runs = parts > 0 ? parts : std::max<int64_t>(1, std::min<int64_t>(8, d->n / 2));
-  split_parts(p, d->n, runs, 1);
   const int64_t e = bytes_of(d->dtype);
+  const int64_t moved = d->n * d->h * d->w * d->c * e + d->k * d->r * d->s * d->c * e +
+                        d->n * pp * qq * d->k * bytes_of(d->dtype_out);
+  const int64_t runs = parts > 0 ? parts : default_parts(moved, d->n);
+  split_parts(p, d->n, runs, 1);
   int rc;
   if ((rc = alloc(&p->a, d->n * d->h * d->w * d->c * e, &p->device_bytes, "input")) ||
       (rc = alloc(&p->b, d->k * d->r * d->s * d->c * e, &p->device_bytes, "weight")) ||

@@ -299,7 +299,8 @@ typedef struct choreo_host_gemm_desc {
   float alpha;
   int32_t has_bias, dtype_bias;
   int32_t relu;
-  int32_t parts;               /* row slabs of A and C; 0 = library choice (~1024-row slabs, at most 16) */
+  int32_t parts;               /* row slabs of A and C; 0 = library choice (every slab moving at least
+                                  40 MiB over the host links, at most 16) */
   int32_t device;              /* CUDA device the plan runs on */
 } choreo_host_gemm_desc;
 
@@ -318,7 +319,8 @@ int choreo_host_gemm_plan_create(const choreo_host_gemm_desc* d, choreo_host_pla
 /* Makes a conv plan for the shape in *d: its data pointers are not used,
  * except that a non-NULL d->bias makes a plan with a bias; alpha, bias type
  * and ReLU are taken from it. The batch is cut into `parts` runs of images
- * (0 = library choice, at most 8). */
+ * (0 = library choice: every run moving at least 40 MiB over the host links,
+ * at most 16). */
 int choreo_host_conv_plan_create(const choreo_conv_desc* d, int32_t parts, int32_t device,
                                  choreo_host_plan** out);
 
