@@ -192,3 +192,28 @@ def test_handover_window_setting_keeps_results(cb, cuda):
             cb.gemm(a, b, c)
         cb.sync_status()
         assert torch.equal(c, ref), w
+
+
+def test_handover_window_setting_keeps_conv_results(cb, cuda, orc):
+    """The same on the implicit-GEMM conv (36 k-blocks per tile, whose default
+    window is one less than the ring depth): every window gives the default's
+    bits, and the default matches the fp64 conv."""
+    import torch
+    n, hh, ww, c, k = 6, 20, 20, 256, 256
+    x = torch.empty(n, hh, ww, c, device="cuda").uniform_(0, 1).half()
+    w = (torch.randn(k, 3, 3, c, device="cuda") / 48).half()
+    bias = (torch.randn(k, device="cuda") * 0.1).half()
+    with cb.tuning(tile="wide256"):
+        ref = torch.empty(n, hh, ww, k, device="cuda", dtype=torch.float16)
+        cb.conv2d(x, w, ref, bias=bias, relu=True)
+    cb.sync_status()
+    for win in (1, 2, 3, 4):
+        with cb.tuning(tile="wide256", handover_kb=win):
+            out = torch.empty_like(ref)
+            cb.conv2d(x, w, out, bias=bias, relu=True)
+        cb.sync_status()
+        assert torch.equal(out, ref), win
+    xb, wb, bb = (t.cpu().view(torch.int16).numpy().view(np.uint16) for t in (x, w, bias))
+    exp = orc.conv2d_f64(xb[:2], wb, F16, bias=bb, dtype_bias=F16, relu=True)
+    got = as_f64(ref[:2].cpu().view(torch.int16).numpy().view(np.uint16), F16).reshape(-1, k)
+    assert_close(got, exp, what="conv, default window", k=9 * c)
