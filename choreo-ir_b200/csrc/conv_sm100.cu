@@ -63,11 +63,12 @@ struct ConvLoader {
     else
       tma_load_3d(dst_b, tb, bar, cb * 64, rs, n0, pol_b);
   }
-  // The wide tile's 256 rows of one CTA: two 128-pixel im2col loads.
+  // The wide tile's 256 rows of one CTA: one im2col load, its tensor map
+  // encoded with 256 pixels per column for the wide tile (the 128-byte
+  // swizzle repeats every 8 rows, so the rows land as two 128-row halves would).
   __device__ __forceinline__ static void issue_a_256(const CUtensorMap* ta, const TcParams& p, int b, int m0,
                                                      int kb, uint32_t dst_a, uint32_t bar, uint64_t pol_a) {
     issue_a(ta, p, b, m0, kb, dst_a, bar, pol_a);
-    issue_a(ta, p, b, m0 + 128, kb, dst_a + 16384, bar, pol_a);
   }
   __device__ __forceinline__ static void issue(const CUtensorMap* ta, const CUtensorMap* tb,
                                                const TcParams& p, int b, int m0, int n0, int kb,
@@ -218,7 +219,9 @@ int launch_conv_tc(const choreo_conv_desc& d, cudaStream_t stream) {
     const int upper[2] = {static_cast<int>(d.pad_w - (d.s - 1) * d.dil_w),
                           static_cast<int>(d.pad_h - (d.r - 1) * d.dil_h)};
     const uint32_t estr[4] = {1, static_cast<uint32_t>(d.stride_w), static_cast<uint32_t>(d.stride_h), 1};
-    int rc = encode_tmap_im2col(&ta, tdt, d.input, dims, strides, lower, upper, 64, kBM, estr);
+    // pixels per load: the wide tile's CTA takes its 256 rows in one load
+    const uint32_t pixels = cfg.wide ? 2 * kBM : kBM;
+    int rc = encode_tmap_im2col(&ta, tdt, d.input, dims, strides, lower, upper, 64, pixels, estr);
     if (rc) return rc;
   }
   {
