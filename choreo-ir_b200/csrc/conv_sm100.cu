@@ -3,10 +3,11 @@
 // GEMM view (NHWC activations, KRSC weights, NHWC output):
 //   M = N*P*Q output pixels, N_gemm = K output channels, K_gemm = R*S*C.
 // K is walked as (r, s, 64-channel block). For each k-block:
-//   A tile (128 pixels x 64 channels) comes from one im2col-mode TMA load:
+//   A tile (128 pixels x 64 channels; 256 for a wide tile's CTA) comes from one
+//     im2col-mode TMA load:
 //     the tensor map's bounding box is the set of filter base positions
 //     (lower corner -pad, upper corner pad - (filter-1)*dilation), the load
-//     starts at the tile's first output pixel and walks 128 pixels through
+//     starts at the tile's first output pixel and walks 128 (256) pixels through
 //     that box (wrapping rows and images), each pixel shifted by the filter
 //     offset (s*dil_w, r*dil_h). Out-of-image pixels and channels >= C read
 //     as zero, which is the zero padding of the convolution.
@@ -76,6 +77,43 @@ struct ConvLoader {
                                                uint64_t pol_a, uint64_t pol_b) {
     issue_a(ta, p, b, m0, kb, dst_a, bar, pol_a);
     issue_b(tb, p, b, n0, kb, dst_b, bar, pol_b);
+  }
+  // The wide tile's per-tile load state: the first output pixel's image and
+  // input corner, decomposed once per tile, and the filter tap and channel
+  // block of the next k-block, stepped as the producer walks k-blocks 0, 1, ...
+  // (channel blocks of one tap, then the next tap) with no division per stage.
+  struct WideCursor {
+    int img, h0, w0, n0;
+    int r, s, cb;
+  };
+  __device__ __forceinline__ static WideCursor wide_cursor(const TcParams& p, int, int m0, int n0) {
+    const int pq = p.conv_p * p.conv_q;
+    const int img = m0 / pq;
+    const int rem = m0 - img * pq;
+    const int op = rem / p.conv_q;
+    const int oq = rem - op * p.conv_q;
+    return WideCursor{img, op * p.conv_stride_h - p.conv_pad_h, oq * p.conv_stride_w - p.conv_pad_w, n0, 0, 0, 0};
+  }
+  __device__ __forceinline__ static void issue_wide(const CUtensorMap* ta, const CUtensorMap* tb, const TcParams& p,
+                                                    WideCursor& c, int, uint32_t dst_a, uint32_t dst_b,
+                                                    uint32_t bar, uint64_t pol_a, uint64_t pol_b) {
+    const uint16_t off_w = static_cast<uint16_t>(c.s * p.conv_dil_w);
+    const uint16_t off_h = static_cast<uint16_t>(c.r * p.conv_dil_h);
+    const int rs = c.r * p.conv_s + c.s;
+    if constexpr (PAIR) {
+      tma_load_im2col_4d_pair(dst_a, ta, bar, c.cb * 64, c.w0, c.h0, c.img, off_w, off_h, pol_a);
+      tma_load_3d_pair(dst_b, tb, bar, c.cb * 64, rs, c.n0, pol_b);
+    } else {
+      tma_load_im2col_4d(dst_a, ta, bar, c.cb * 64, c.w0, c.h0, c.img, off_w, off_h, pol_a);
+      tma_load_3d(dst_b, tb, bar, c.cb * 64, rs, c.n0, pol_b);
+    }
+    if (++c.cb == p.conv_c_blocks) {
+      c.cb = 0;
+      if (++c.s == p.conv_s) {
+        c.s = 0;
+        ++c.r;
+      }
+    }
   }
 };
 

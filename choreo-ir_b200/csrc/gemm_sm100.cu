@@ -87,6 +87,20 @@ struct GemmLoader {
     issue_a(ta, p, b, m0, kb, dst_a, bar, pol_a);
     issue_b(tb, p, b, n0, kb, dst_b, bar, pol_b);
   }
+  // The wide tile's per-tile load state: the tile's coordinates.
+  struct WideCursor {
+    int b, m0, n0;
+  };
+  __device__ __forceinline__ static WideCursor wide_cursor(const TcParams&, int b, int m0, int n0) {
+    return WideCursor{b, m0, n0};
+  }
+  // k-block kb of a wide tile: this CTA's 256 A rows and its B columns.
+  __device__ __forceinline__ static void issue_wide(const CUtensorMap* ta, const CUtensorMap* tb, const TcParams& p,
+                                                    WideCursor& c, int kb, uint32_t dst_a, uint32_t dst_b,
+                                                    uint32_t bar, uint64_t pol_a, uint64_t pol_b) {
+    issue_a_256(ta, p, c.b, c.m0, kb, dst_a, bar, pol_a);
+    issue_b(tb, p, c.b, c.n0, kb, dst_b, bar, pol_b);
+  }
 };
 
 }  // namespace choreo_sm100

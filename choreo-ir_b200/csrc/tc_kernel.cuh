@@ -518,6 +518,10 @@ constexpr int tc_smem_bytes() {
 //                                uint32_t bar, uint64_t pol_a, uint64_t pol_b);
 // loads this CTA's A rows [m0, m0 + 128) and B columns [n0, n0 + B width) for
 // k-block kb of batch item b into the stage at dst_a / dst_b, counted on bar.
+// The wide tile's producer uses a per-tile cursor instead:
+//   struct WideCursor;  static WideCursor wide_cursor(const TcParams&, int b, int m0, int n0);
+//   static void issue_wide(ta, tb, p, WideCursor&, int kb, dst_a, dst_b, bar, pol_a, pol_b);
+// called for k-blocks 0, 1, ... of one tile in order (this CTA's 256 A rows).
 template <int BN, int STAGES, class Loader, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
@@ -997,6 +1001,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tile_coords(t, p, b, mb, nb);
         const int m0 = mb * (4 * kBM) + static_cast<int>(rank) * (2 * kBM);  // this CTA's 256 rows
         const int n0 = nb * BN + static_cast<int>(rank) * BNL;
+        auto cur = Loader::wide_cursor(p, b, m0, n0);  // per-tile load state; k-blocks in order
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
           if (!mbar_wait(smem_u32(&bars->empty[stage]), phase ^ 1, wctx, kStatusTimeoutProducer)) {
             ok = false;
@@ -1005,9 +1010,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t own_full = smem_u32(&bars->full[stage]);
           if (leader) mbar_arrive_expect_tx(own_full, 2 * kStageBytes);
           const uint32_t bar = mapa_shared(own_full, 0);
-          const uint32_t a_dst = smem_u32(s_a + stage * kAStage);
-          Loader::issue_a_256(&tma_a, p, b, m0, kb, a_dst, bar, pol_a);
-          Loader::issue_b(&tma_b, p, b, n0, kb, smem_u32(s_b + stage * kBStage), bar, pol_b);
+          Loader::issue_wide(&tma_a, &tma_b, p, cur, kb, smem_u32(s_a + stage * kAStage),
+                             smem_u32(s_b + stage * kBStage), bar, pol_a, pol_b);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
