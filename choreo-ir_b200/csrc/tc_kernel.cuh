@@ -67,8 +67,8 @@ struct TcParams {
   // failure reporting
   uint32_t* status;
   uint64_t timeout_ns;
-  // wide tile: k-blocks replayed around each accumulator hand-over (0 = the
-  // pipeline depth)
+  // wide tile: k-blocks one accumulator half runs alone at each hand-over
+  // (0 = library choice; see wide_head_kb)
   int32_t handover_kb;
   // measurement hook (null = off): CTA 0 adds the SM clock cycles and the
   // %globaltimer nanoseconds of its lifetime to [0] and [1], and 1 to [2]
@@ -909,12 +909,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // each CTA. Each CTA keeps its 256 x 256 fp32 accumulator (128 rows of each
 // half) in all 512 TMEM columns: a quarter less L2 -> SM operand traffic per
 // FLOP than 256 x 256 tiles. With no room for a second accumulator, overlap
-// comes from handing the accumulator over in halves at both ends of a tile:
-// the last pipeline-depth k-blocks issue their half-0 MMAs first and publish
-// half 0, so the epilogue reads it out while the same stages are replayed for
-// half 1; the epilogue releases each half as soon as it has read it into
-// registers, and the next tile's first pipeline-depth k-blocks issue their
-// half-0 MMAs while half 1 is being read.
+// comes from handing the accumulator over in halves: a tile's first D
+// k-blocks run for half 0 alone while the epilogue reads the previous tile's
+// half 1 out; then both halves run over k-blocks D .. K-1, half 0 is published,
+// and half 1 finishes over k-blocks 0 .. D-1, which the producer loads a
+// second time, while the epilogue reads half 0 out. No stage is held across a
+// hand-over, so the ring keeps streaming over tile boundaries (holding the
+// window's stages instead left the 4-stage ring to refill twice per tile).
+// Tiles no longer than the window hold their stages and replay them.
 template <int STAGES>
 struct alignas(8) TcWideBarriers {
   uint64_t full[STAGES];
@@ -926,6 +928,20 @@ struct alignas(8) TcWideBarriers {
   uint32_t tmem_base;
   int32_t abort;
 };
+
+// The wide tile's hand-over window D: k-blocks half 0 runs alone at the head
+// of a tile (and half 1 at its end). choreo_tuning::handover_kb when in
+// 1 .. 16, else the ring depth, one less for tiles under 64 k-blocks. A tile
+// of no more k-blocks than that holds its stages (D = K) when they fit the
+// ring, and otherwise streams with D = the ring depth. Producer and MMA issuer
+// both use it.
+__device__ __forceinline__ int wide_head_kb(const TcParams& p, int stages) {
+  const int w = p.handover_kb > 0 && p.handover_kb <= 16
+                    ? p.handover_kb
+                    : (p.num_k_blocks < 64 && stages > 2 ? stages - 1 : stages);
+  if (p.num_k_blocks > w) return w;
+  return p.num_k_blocks <= stages ? p.num_k_blocks : stages;
+}
 
 template <int STAGES>
 constexpr int tc_wide_smem_bytes() {
@@ -1001,8 +1017,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tile_coords(t, p, b, mb, nb);
         const int m0 = mb * (4 * kBM) + static_cast<int>(rank) * (2 * kBM);  // this CTA's 256 rows
         const int n0 = nb * BN + static_cast<int>(rank) * BNL;
+        // k-blocks 0 .. K-1, then 0 .. D-1 again for half 1 when the tile is
+        // longer than the hand-over window (see the MMA issuer)
+        const int D = wide_head_kb(p, STAGES);
+        const int loads = p.num_k_blocks + (D < p.num_k_blocks ? D : 0);
         auto cur = Loader::wide_cursor(p, b, m0, n0);  // per-tile load state; k-blocks in order
-        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+        for (int i = 0; i < loads; ++i) {
+          if (i == p.num_k_blocks) cur = Loader::wide_cursor(p, b, m0, n0);
+          const int kb = i < p.num_k_blocks ? i : i - p.num_k_blocks;
           if (!mbar_wait(smem_u32(&bars->empty[stage]), phase ^ 1, wctx, kStatusTimeoutProducer)) {
             ok = false;
             break;
@@ -1036,8 +1058,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (leader && lane == 0) {
       const uint32_t idesc = idesc_f16(2 * kBM, BN, p.ab_bf16 != 0, Loader::kAMn, Loader::kBMn);
-      // The MMAs of one accumulator half for one stage.
-      auto issue_half = [&](int h, uint32_t st, int kb) {
+      // The MMAs of one accumulator half for one stage; `first` starts the sum.
+      auto issue_half = [&](int h, uint32_t st, bool first) {
         const uint32_t ah = smem_u32(s_a + st * kAStage) + h * kAHalf;
         const uint32_t b0 = smem_u32(s_b + st * kBStage);
 #pragma unroll
@@ -1046,7 +1068,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                            : smem_desc_sw128(ah + k * 32, 16, 1024);
           const uint64_t bd = Loader::kBMn ? smem_desc_sw128(b0 + k * 2048, 8192, 1024)
                                            : smem_desc_sw128(b0 + k * 32, 16, 1024);
-          umma_f16_pair(tmem_base + h * BN, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_f16_pair(tmem_base + h * BN, ad, bd, idesc, (first && k == 0) ? 0u : 1u);
         }
       };
       auto release = [&](uint32_t st) {
@@ -1056,88 +1078,99 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       };
       uint32_t stage = 0, phase = 0, local = 0;
       bool ok = true;
+      auto publish = [&](int h) {  // half h of the tile is complete once its MMAs finish
+        const uint32_t fb = smem_u32(&bars->tmem_full[h]);
+        umma_commit_pair(fb);
+        umma_commit_pair(mapa_shared(fb, 1));
+      };
+      auto wait_full = [&](uint32_t st, uint32_t ph) {
+        if (!mbar_wait(smem_u32(&bars->full[st]), ph, wctx, kStatusTimeoutMma)) return false;
+        tc_fence_after();
+        return true;
+      };
+      auto advance = [&] {
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      };
+      const int K = p.num_k_blocks;
+      const int D = wide_head_kb(p, STAGES);
       for (int64_t t = cluster_id; t < p.num_tiles && ok; t += num_clusters, ++local) {
         const uint32_t tph = local & 1;
-        // Head of the tile: the first D stages (already prefetched while the
-        // previous tile's epilogue ran) are consumed for half 0 as soon as the
-        // epilogue has read half 0 out, and replayed for half 1 (then
-        // released) once it has read half 1 — the half-1 drain overlaps
-        // D k-blocks of half-0 MMAs. The window defaults to the ring depth, one
-        // less for tiles under 64 k-blocks, whose stage refill at each tile
-        // boundary weighs more than a shorter overlap.
-        const int W = p.handover_kb > 0 && p.handover_kb < STAGES
-                          ? p.handover_kb
-                          : (p.num_k_blocks < 64 && STAGES > 2 ? STAGES - 1 : STAGES);
-        const int D = p.num_k_blocks < W ? p.num_k_blocks : W;
         if (!mbar_wait(smem_u32(&bars->tmem_empty[0]), tph ^ 1, wctx, kStatusTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint32_t st = stage, ph = phase;
-        for (int kb = 0; kb < D; ++kb) {
-          if (!mbar_wait(smem_u32(&bars->full[st]), ph, wctx, kStatusTimeoutMma)) {
+        if (D == K) {
+          // The whole tile fits the window: its stages are held after the
+          // half-0 MMAs, replayed for half 1 once the epilogue has read the
+          // previous tile's half 1, and released then.
+          uint32_t st = stage, ph = phase;
+          for (int kb = 0; kb < K; ++kb) {
+            if (!wait_full(st, ph)) {
+              ok = false;
+              break;
+            }
+            issue_half(0, st, kb == 0);
+            if (++st == STAGES) { st = 0; ph ^= 1; }
+          }
+          if (!ok) break;
+          publish(0);
+          if (!mbar_wait(smem_u32(&bars->tmem_empty[1]), tph ^ 1, wctx, kStatusTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_half(0, st, kb);
-          if (++st == STAGES) { st = 0; ph ^= 1; }
+          for (int kb = 0; kb < K; ++kb) {
+            issue_half(1, stage, kb == 0);
+            release(stage);
+            advance();
+          }
+          publish(1);
+          continue;
+        }
+        // Head: k-blocks 0 .. D-1 for half 0 while the epilogue reads the
+        // previous tile's half 1 out. Each stage is released at once, so the
+        // ring keeps streaming across the tile boundary; the producer loads
+        // these k-blocks again after the tile's last one, for half 1.
+        for (int kb = 0; kb < D; ++kb) {
+          if (!wait_full(stage, phase)) {
+            ok = false;
+            break;
+          }
+          issue_half(0, stage, kb == 0);
+          release(stage);
+          advance();
         }
         if (!ok) break;
-        auto publish = [&](int h) {  // half h of the tile is complete once its MMAs finish
-          const uint32_t fb = smem_u32(&bars->tmem_full[h]);
-          umma_commit_pair(fb);
-          umma_commit_pair(mapa_shared(fb, 1));
-        };
-        if (D == p.num_k_blocks) publish(0);
         if (!mbar_wait(smem_u32(&bars->tmem_empty[1]), tph ^ 1, wctx, kStatusTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        for (int kb = 0; kb < D; ++kb) {
-          issue_half(1, stage, kb);
-          release(stage);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
-        }
-        // Steady state: both halves per stage, up to the tail.
-        const int T = (p.num_k_blocks - D) < W ? (p.num_k_blocks - D) : W;
-        for (int kb = D; kb < p.num_k_blocks - T; ++kb) {
-          if (!mbar_wait(smem_u32(&bars->full[stage]), phase, wctx, kStatusTimeoutMma)) {
+        // Body: both halves per stage; half 1's sum starts at k-block D.
+        for (int kb = D; kb < K; ++kb) {
+          if (!wait_full(stage, phase)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          issue_half(0, stage, kb);
-          issue_half(1, stage, kb);
+          issue_half(0, stage, false);
+          issue_half(1, stage, kb == D);
           release(stage);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          advance();
         }
         if (!ok) break;
-        // Tail: the last T stages are consumed for half 0, which is then
-        // published so the epilogue drains it while the same stages are
-        // replayed for half 1 — the half-0 drain overlaps T k-blocks of MMAs.
-        if (T > 0) {
-          st = stage;
-          ph = phase;
-          for (int kb = p.num_k_blocks - T; kb < p.num_k_blocks; ++kb) {
-            if (!mbar_wait(smem_u32(&bars->full[st]), ph, wctx, kStatusTimeoutMma)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_half(0, st, kb);
-            if (++st == STAGES) { st = 0; ph ^= 1; }
+        publish(0);  // read out by the epilogue during the replay below
+        // Replay: k-blocks 0 .. D-1 again, for half 1.
+        for (int kb = 0; kb < D; ++kb) {
+          if (!wait_full(stage, phase)) {
+            ok = false;
+            break;
           }
-          if (!ok) break;
-          publish(0);
-          for (int kb = p.num_k_blocks - T; kb < p.num_k_blocks; ++kb) {
-            issue_half(1, stage, kb);
-            release(stage);
-            if (++stage == STAGES) { stage = 0; phase ^= 1; }
-          }
+          issue_half(1, stage, false);
+          release(stage);
+          advance();
         }
+        if (!ok) break;
         publish(1);
       }
       umma_commit_pair(smem_u32(&bars->drain));

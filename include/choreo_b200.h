@@ -168,9 +168,9 @@ typedef struct choreo_tuning {
   int32_t l2_policy_b;      /* -1 = default (normal); same codes */
   double wait_timeout_ms;   /* 0 = default 2000: limit of every bounded pipeline wait */
   int32_t handover_kb;      /* 512 x 256 tiles: k-blocks the MMA issuer runs for one accumulator
-                               half while the other is handed over, at each end of a tile
-                               (0 = the pipeline depth, one less for tiles of fewer than
-                               64 k-blocks) */
+                               half alone while the other is handed over, at each end of a
+                               tile (1..16; 0 = the pipeline depth, one less for tiles of
+                               fewer than 64 k-blocks) */
   int32_t reserved;
 } choreo_tuning;
 

@@ -175,45 +175,65 @@ def test_clock_probe_counts_launches_and_reads_a_plausible_clock(cb, cuda):
     assert cb.lib.choreo_clock_probe_set(probe.data_ptr() + 4) == cb.ERR_INVALID_ARG  # 8-byte alignment
 
 
-def test_handover_window_setting_keeps_results(cb, cuda):
-    """The wide tile's hand-over window (choreo_tuning::handover_kb) changes the
-    order MMAs are issued in, never the sums: every setting gives the same
-    bits as the default."""
+def _half0_rows(m):
+    """Rows of a 512 x 256 tile that accumulator half 0 holds: the first 128 of
+    each CTA's 256."""
+    return np.arange(m) % 256 < 128
+
+
+def test_handover_window_setting(cb, cuda, orc):
+    """The wide tile's hand-over window (choreo_tuning::handover_kb): half 0
+    sums k-blocks 0 .. K-1 in order whatever the window, so its rows have the
+    same bits for every setting; half 1 sums k-blocks D .. K-1 and then 0 .. D-1,
+    so its rows agree with the fp64 product within the tolerance; every setting
+    repeats its own bits."""
     import torch
-    m, n, k = 1536, 1024, 2048
-    a = torch.empty(m, k, device="cuda", dtype=torch.float16).uniform_(-1, 1)
-    b = torch.empty(k, n, device="cuda", dtype=torch.float16).uniform_(-1, 1)
+    m, n, k = 1024, 512, 2048
+    g = torch.Generator().manual_seed(3)
+    a16 = torch.empty(m, k).uniform_(-1, 1, generator=g).half()
+    b16 = torch.empty(k, n).uniform_(-1, 1, generator=g).half()
+    a, b = a16.cuda(), b16.cuda()
     with cb.tuning(tile="wide256"):
         ref = torch.empty(m, n, device="cuda", dtype=torch.float16)
         cb.gemm(a, b, ref)
+    cb.sync_status()
+    h0 = torch.from_numpy(_half0_rows(m)).cuda()
+    exp = orc.gemm_f64(_bits(a16), _bits(b16), F16)
     for w in (1, 2, 3, 4, 9):
-        with cb.tuning(tile="wide256", handover_kb=w):
-            c = torch.empty_like(ref)
-            cb.gemm(a, b, c)
-        cb.sync_status()
-        assert torch.equal(c, ref), w
+        outs = []
+        for _ in range(2):
+            with cb.tuning(tile="wide256", handover_kb=w):
+                c = torch.empty_like(ref)
+                cb.gemm(a, b, c)
+            cb.sync_status()
+            outs.append(c)
+        assert torch.equal(outs[0], outs[1]), w
+        assert torch.equal(outs[0][h0], ref[h0]), w
+        assert_close(as_f64(_bits(outs[0].cpu()), F16), exp, what=f"GEMM, window {w}", k=k)
 
 
-def test_handover_window_setting_keeps_conv_results(cb, cuda, orc):
-    """The same on the implicit-GEMM conv (36 k-blocks per tile, whose default
-    window is one less than the ring depth): every window gives the default's
-    bits, and the default matches the fp64 conv."""
+def test_handover_window_setting_conv(cb, cuda, orc):
+    """The same on the implicit-GEMM conv (36 k-blocks per tile): half-0 pixels
+    have the default's bits for every window, and each window's output matches
+    the fp64 conv."""
     import torch
     n, hh, ww, c, k = 6, 20, 20, 256, 256
-    x = torch.empty(n, hh, ww, c, device="cuda").uniform_(0, 1).half()
-    w = (torch.randn(k, 3, 3, c, device="cuda") / 48).half()
-    bias = (torch.randn(k, device="cuda") * 0.1).half()
+    g = torch.Generator().manual_seed(4)
+    x16 = torch.empty(n, hh, ww, c).uniform_(0, 1, generator=g).half()
+    w16 = (torch.randn(k, 3, 3, c, generator=g) / 48).half()
+    b16 = (torch.randn(k, generator=g) * 0.1).half()
+    x, w, bias = x16.cuda(), w16.cuda(), b16.cuda()
     with cb.tuning(tile="wide256"):
         ref = torch.empty(n, hh, ww, k, device="cuda", dtype=torch.float16)
         cb.conv2d(x, w, ref, bias=bias, relu=True)
     cb.sync_status()
+    pix = n * hh * ww
+    h0 = torch.from_numpy(_half0_rows(pix)).cuda()
+    exp = orc.conv2d_f64(_bits(x16), _bits(w16), F16, bias=_bits(b16), dtype_bias=F16, relu=True)
     for win in (1, 2, 3, 4):
         with cb.tuning(tile="wide256", handover_kb=win):
             out = torch.empty_like(ref)
             cb.conv2d(x, w, out, bias=bias, relu=True)
         cb.sync_status()
-        assert torch.equal(out, ref), win
-    xb, wb, bb = (t.cpu().view(torch.int16).numpy().view(np.uint16) for t in (x, w, bias))
-    exp = orc.conv2d_f64(xb[:2], wb, F16, bias=bb, dtype_bias=F16, relu=True)
-    got = as_f64(ref[:2].cpu().view(torch.int16).numpy().view(np.uint16), F16).reshape(-1, k)
-    assert_close(got, exp, what="conv, default window", k=9 * c)
+        assert torch.equal(out.view(pix, k)[h0], ref.view(pix, k)[h0]), win
+        assert_close(as_f64(_bits(out.cpu()), F16).reshape(-1, k), exp, what=f"conv, window {win}", k=9 * c)
