@@ -237,3 +237,46 @@ def test_handover_window_setting_conv(cb, cuda, orc):
         cb.sync_status()
         assert torch.equal(out.view(pix, k)[h0], ref.view(pix, k)[h0]), win
         assert_close(as_f64(_bits(out.cpu()), F16).reshape(-1, k), exp, what=f"conv, window {win}", k=9 * c)
+
+
+@pytest.mark.parametrize("kblocks", [1, 2, 3, 4, 5, 6, 9])
+def test_wide_tile_handover_paths(cb, cuda, orc, kblocks):
+    """The 512 x 256 tile's hand-over paths across K: tiles no longer than the
+    window hold and replay their stages (K <= ring depth), longer ones stream
+    (head for half 0, body for both, second load of the head for half 1), and
+    a window above the ring depth streams with the ring depth; bias + ReLU
+    and a ragged M and N edge, each against fp64."""
+    import torch
+    m, n, k = 1100, 520, 64 * kblocks
+    g = torch.Generator().manual_seed(100 + kblocks)
+    a = torch.empty(m, k).uniform_(-1, 1, generator=g).bfloat16()
+    b = torch.empty(k, n).uniform_(-1, 1, generator=g).bfloat16()
+    bias = torch.empty(n).normal_(0, 0.3, generator=g).bfloat16()
+    exp = orc.gemm_f64(_bits(a), _bits(b), BF16, bias=_bits(bias), dtype_bias=BF16, relu=True)
+    ad, bd, biasd = a.cuda(), b.cuda(), bias.cuda()
+    for win in (0, 2, 5, 16):
+        with cb.tuning(tile="wide256", handover_kb=win):
+            c = torch.full((m, n), 7.0, device="cuda", dtype=torch.bfloat16)
+            cb.gemm(ad, bd, c, bias=biasd, relu=True)
+        cb.sync_status()
+        assert_close(as_f64(_bits(c.cpu()), BF16), exp, what=f"wide tile, {kblocks} k-blocks, window {win}", k=k)
+
+
+@pytest.mark.parametrize("c_in,r", [(256, 1), (320, 1), (64, 3)])
+def test_wide_tile_conv_handover_paths(cb, cuda, orc, c_in, r):
+    """The conv's 512 x 256 tile on both sides of the window: 4 k-blocks (1x1,
+    256 channels) hold, 5 (1x1, 320 channels: the last block part past C)
+    stream with a 3-k-block window, 9 (3x3, 64 channels) stream; against fp64."""
+    import torch
+    n, hh, ww, k = 3, 14, 14, 256
+    g = torch.Generator().manual_seed(c_in + r)
+    x = torch.empty(n, hh, ww, c_in).uniform_(0, 1, generator=g).half()
+    w = (torch.randn(k, r, r, c_in, generator=g) / np.sqrt(r * r * c_in)).half()
+    bias = (torch.randn(k, generator=g) * 0.1).half()
+    pad = r // 2
+    exp = orc.conv2d_f64(_bits(x), _bits(w), F16, pad=pad, bias=_bits(bias), dtype_bias=F16, relu=True)
+    with cb.tuning(tile="wide256"):
+        out = torch.empty(n, hh, ww, k, device="cuda", dtype=torch.float16)
+        cb.conv2d(x.cuda(), w.cuda(), out, padding=pad, bias=bias.cuda(), relu=True)
+    cb.sync_status()
+    assert_close(as_f64(_bits(out.cpu()), F16).reshape(-1, k), exp, what=f"wide conv C={c_in} {r}x{r}", k=r * r * c_in)
