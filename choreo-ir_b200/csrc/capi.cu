@@ -446,8 +446,8 @@ int choreo_tuning_set(const choreo_tuning* t) {
       return fail(CHOREO_ERR_INVALID_ARG, "tuning: L2 policy codes are -1, 0, 1 or 2");
     if (!(v.wait_timeout_ms >= 0.0) || v.wait_timeout_ms > 3.6e6)
       return fail(CHOREO_ERR_INVALID_ARG, "tuning: wait_timeout_ms outside 0..3.6e6");
-    if (v.handover_kb < 0 || v.handover_kb > 64)
-      return fail(CHOREO_ERR_INVALID_ARG, "tuning: handover_kb %d outside 0..64", v.handover_kb);
+    if (v.handover_kb < 0 || v.handover_kb > 16)
+      return fail(CHOREO_ERR_INVALID_ARG, "tuning: handover_kb %d outside 0..16", v.handover_kb);
     v.reserved = 0;
   }
   {

@@ -226,13 +226,15 @@ def test_tuning_defaults_roundtrip_and_validation(cb):
     assert cb.lib.choreo_tuning_set(None) == 0
     d = cb.get_tuning()
     assert (d.tile, d.split_k, d.group_m, d.l2_policy_a, d.l2_policy_b, d.wait_timeout_ms) == (b"", 0, 0, -1, -1, 0.0)
-    with cb.tuning(tile="single128", split_k=4, group_m=8, l2_policy_a=2, l2_policy_b=1, wait_timeout_ms=250.0):
+    with cb.tuning(tile="single128", split_k=4, group_m=8, l2_policy_a=2, l2_policy_b=1, wait_timeout_ms=250.0,
+                   handover_kb=16):
         t = cb.get_tuning()
-        assert (t.tile, t.split_k, t.group_m, t.l2_policy_a, t.l2_policy_b, t.wait_timeout_ms) == \
-            (b"single128", 4, 8, 2, 1, 250.0)
+        assert (t.tile, t.split_k, t.group_m, t.l2_policy_a, t.l2_policy_b, t.wait_timeout_ms, t.handover_kb) == \
+            (b"single128", 4, 8, 2, 1, 250.0, 16)
         for bad, msg in [(dict(tile="huge512"), "unknown tile"), (dict(split_k=65), "split_k"),
                          (dict(group_m=-1), "group_m"), (dict(l2_policy_a=3), "L2 policy"),
-                         (dict(wait_timeout_ms=-1.0), "wait_timeout_ms")]:
+                         (dict(wait_timeout_ms=-1.0), "wait_timeout_ms"), (dict(handover_kb=17), "handover_kb"),
+                         (dict(handover_kb=-1), "handover_kb")]:
             with pytest.raises(cb.ChoreoError, match=msg):
                 cb.set_tuning(**bad)
         assert cb.get_tuning().tile == b"single128"  # unchanged by the refused calls
