@@ -138,6 +138,16 @@ def shard_rows(m: int, world: int, rank: int) -> tuple[int, int]:
     return r0, r1 - r0
 
 
+def b_rows_share(k: int, world: int, rank: int) -> tuple[int, int, int]:
+    """The rows of B (K x N) rank `rank` copies from the host when B crosses
+    PCIe once for the whole job: (share, k0, k1) with `share` rows per rank
+    (the last ranks' tails empty when world does not divide K) and this rank's
+    rows [k0, k1). An all-gather of the `share`-row parts assembles B's K rows
+    at the head of a world * share row buffer on every rank."""
+    share = -(-k // world)
+    return share, min(rank * share, k), min((rank + 1) * share, k)
+
+
 def conv_images(n: int, world: int, rank: int) -> tuple[int, int]:
     """This rank's contiguous run of images (first, count): the batch split
     evenly, the first n % world ranks taking one extra."""
@@ -534,10 +544,9 @@ def setup_gemm(cb, spec, world, rank, dev, stream) -> Case:
     else:
         # B crosses PCIe once for the whole job: each rank copies 1/world of
         # B's rows, and an NCCL all-gather over NVLink assembles B everywhere.
-        share = -(-K // world)
+        share, k0, k1 = b_rows_share(K, world, rank)
         b_full = torch.empty(share * world, N, device=dev, dtype=dt)
         b_part = torch.empty(share, N, device=dev, dtype=dt)
-        k0, k1 = min(rank * share, K), min((rank + 1) * share, K)
         bias_d = torch.empty_like(bias) if bias is not None else None
 
         def e2e():

@@ -123,6 +123,60 @@ def test_failed_rank_is_detected_not_hung(tmp_path):
     assert (tmp_path / "rank0_error").exists()
 
 
+def _b_once_worker(rank: int, world: int, port: int, k: int, out_dir: str) -> None:
+    """bench.py's B-once end-to-end step on gloo ranks: each rank copies its
+    rows of the host B (b_rows_share) into a share-row part, and the
+    all-gather the bench uses assembles every rank's copy of B."""
+    sys.path.insert(0, str(ROOT))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    import bench
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
+    n = 24
+    b_h = (torch.arange(k * n, dtype=torch.float32).reshape(k, n) % 251).to(torch.bfloat16)
+    share, k0, k1 = bench.b_rows_share(k, world, rank)
+    b_full = torch.full((share * world, n), -1.0, dtype=torch.bfloat16)
+    b_part = torch.zeros(share, n, dtype=torch.bfloat16)
+    if k1 > k0:
+        b_part[:k1 - k0].copy_(b_h[k0:k1])
+    dist.all_gather_into_tensor(b_full, b_part)
+    ok = torch.equal(b_full[:k], b_h)
+    Path(out_dir, f"bonce{rank}").write_text("ok" if ok else "mismatch")
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,k", [(2, 8192), (3, 200), (4, 130), (4, 5)])
+def test_bench_b_once_assembles_b_on_every_rank(tmp_path, world, k):
+    """At N > 1 the bench's end-to-end step brings B over PCIe once for the
+    whole job (1/N of its rows per rank) and assembles it by an all-gather:
+    every rank ends with B's K rows, also when N does not divide K and the
+    last rank's share is short or empty."""
+    import torch.multiprocessing as mp
+    sys.path.insert(0, str(ROOT))
+    import bench
+    shares = [bench.b_rows_share(k, world, r) for r in range(world)]
+    assert shares[0][1] == 0 and shares[-1][2] == k
+    assert all(shares[r][2] == shares[r + 1][1] for r in range(world - 1))
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_b_once_worker, args=(r, world, port, k, str(tmp_path))) for r in range(world)]
+    for pr in procs:
+        pr.start()
+    for pr in procs:
+        pr.join(timeout=120)
+        if pr.is_alive():
+            pr.kill()
+            pr.join()
+    assert [pr.exitcode for pr in procs] == [0] * world
+    assert all((tmp_path / f"bonce{r}").read_text() == "ok" for r in range(world))
+
+
 def test_bench_workload_specs():
     sys.path.insert(0, str(ROOT))
     import bench
